@@ -1,0 +1,357 @@
+// capi.cu -- extern "C" entry points (include/iwhisper_b200.h).
+//
+// Argument checking mirrors the TORCH_CHECKs of the reference torch
+// wrappers (i_whisper/kernels/csrc/*/*_torch.cpp); every failure returns a
+// negative code and records a message for iw_last_error().
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/iwhisper_b200.h"
+#include "gemm_i8.cuh"
+#include "iw_common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_check(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return IW_OK;
+    return fail(IW_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+bool ln_width_ok(int64_t d) { return d == 384 || d == 512 || d == 768 || d == 1024 || d == 1280; }
+
+// Stream-ordered scratch buffer, released on the same stream.
+struct Scratch {
+    void *p = nullptr;
+    cudaStream_t st;
+    explicit Scratch(cudaStream_t s) : st(s) {}
+    cudaError_t alloc(size_t bytes) { return cudaMallocAsync(&p, bytes ? bytes : 16, st); }
+    ~Scratch() {
+        if (p) cudaFreeAsync(p, st);
+    }
+};
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Shared body of Linear8 / Linear32 / accum / fused residual: pads K to a
+// multiple of 16 when needed (TMA row-stride rule), computes the row sums
+// of x when a zero point is given, then runs the tcgen05 GEMM.
+int run_linear(const int8_t *x, const int8_t *w, const int32_t *bias, const int8_t *wz, const uint32_t *mult,
+               const int8_t *shift, void *y, int64_t M, int64_t K, int64_t N, iw::EpiMode mode, const int16_t *res,
+               uint16_t res_mult, cudaStream_t st, const char *name) {
+    if (M < 0 || N <= 0) return fail(IW_EINVAL, "%s: invalid shape M=%lld N=%lld", name, (long long)M, (long long)N);
+    if (K <= 0) return fail(IW_EINVAL, "%s: x.size(-1) must be greater than 0", name);
+    if (M == 0) return IW_OK;
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(IW_EINVAL, "%s: dimension too large", name);
+    Scratch xs(st), ws(st), rs(st);
+    const int8_t *xg = x, *wg = w;
+    int64_t Kp = K;
+    if (K % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15)) {
+        Kp = round_up(K, 16);
+        if (int r = cuda_check(xs.alloc((size_t)M * Kp), name)) return r;
+        if (int r = cuda_check(ws.alloc((size_t)N * Kp), name)) return r;
+        if (int r = cuda_check(iw::pad_rows(x, M, K, (int8_t *)xs.p, Kp, st), name)) return r;
+        if (int r = cuda_check(iw::pad_rows(w, N, K, (int8_t *)ws.p, Kp, st), name)) return r;
+        xg = (const int8_t *)xs.p;
+        wg = (const int8_t *)ws.p;
+    }
+    iw::EpiParams p;
+    p.out = y;
+    p.ldo = N;
+    p.bias = bias;
+    p.wz = wz;
+    p.mult = mult;
+    p.shift = shift;
+    p.per_channel = 1;
+    if (wz) {
+        if (int r = cuda_check(rs.alloc((size_t)M * 4), name)) return r;
+        if (int r = cuda_check(iw::rowsum_i8(xg, Kp, (int)M, (int)Kp, (int32_t *)rs.p, st), name)) return r;
+        p.rowsum = (const int32_t *)rs.p;
+    }
+    if (mode == iw::EPI_L32_RES) {
+        p.res = res;
+        p.ldr = N;
+        p.res_mult = res_mult;
+    }
+    iw::GemmShape g{xg, Kp, wg, Kp, (int)M, (int)N, (int)Kp};
+    return cuda_check(iw::gemm_i8_launch(g, mode, p, st), name);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *iw_last_error(void) { return g_err.c_str(); }
+
+int iw_abi_version(void) { return 1; }
+
+int iw_device_status(uint32_t *status, int clear) {
+    if (int r = cuda_check(cudaDeviceSynchronize(), "iw_device_status")) return r;
+    uint32_t v = 0;
+    if (int r = cuda_check(cudaMemcpyFromSymbol(&v, iw::g_device_status, sizeof(v)), "iw_device_status")) return r;
+    if (status) *status = v;
+    if (clear) {
+        const uint32_t z = 0;
+        if (int r = cuda_check(cudaMemcpyToSymbol(iw::g_device_status, &z, sizeof(z)), "iw_device_status")) return r;
+    }
+    return IW_OK;
+}
+
+int iw_linear8(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+               const uint32_t *multiplier, const int8_t *shift, int8_t *y, int64_t M, int64_t K, int64_t N,
+               void *stream) {
+    return run_linear(x, weight, bias, weight_zero, multiplier, shift, y, M, K, N, iw::EPI_L8, nullptr, 0, S(stream),
+                      "iw_linear8");
+}
+
+int iw_linear8_accum(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                     int32_t *y, int64_t M, int64_t K, int64_t N, void *stream) {
+    return run_linear(x, weight, bias, weight_zero, nullptr, nullptr, y, M, K, N, iw::EPI_ACC32, nullptr, 0,
+                      S(stream), "iw_linear8_accum");
+}
+
+int iw_linear32(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                const uint32_t *multiplier, const int8_t *shift, int32_t *y, int64_t M, int64_t K, int64_t N,
+                void *stream) {
+    return run_linear(x, weight, bias, weight_zero, multiplier, shift, y, M, K, N, iw::EPI_L32, nullptr, 0, S(stream),
+                      "iw_linear32");
+}
+
+int iw_linear32_residual15(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                           const uint32_t *multiplier, const int8_t *shift, const int16_t *residual,
+                           uint16_t residual_multiplier, int16_t *y, int64_t M, int64_t K, int64_t N, void *stream) {
+    if (!residual) return fail(IW_EINVAL, "iw_linear32_residual15: residual is required");
+    return run_linear(x, weight, bias, weight_zero, multiplier, shift, y, M, K, N, iw::EPI_L32_RES, residual,
+                      residual_multiplier, S(stream), "iw_linear32_residual15");
+}
+
+int iw_residual15(const int32_t *branch, const int16_t *residual, uint16_t multiplier, int16_t *y, int64_t numel,
+                  void *stream) {
+    if (numel < 0) return fail(IW_EINVAL, "iw_residual15: invalid numel");
+    return cuda_check(iw::residual15(branch, residual, multiplier, y, numel, S(stream)), "iw_residual15");
+}
+
+int iw_layernorm32(const int16_t *x, const int8_t *weight, const int32_t *bias, uint8_t ln_multiplier,
+                   int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y, int64_t rows, int64_t d,
+                   void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    if (rows < 0 || rows > INT32_MAX) return fail(IW_EINVAL, "iw_layernorm32: invalid row count");
+    iw::LnParams p{(int32_t)ln_multiplier, (int32_t)ln_shift, out_multiplier, (uint32_t)(int32_t)out_shift, 13u};
+    return cuda_check(iw::layernorm32(x, d, weight, bias, p, y, d, (int)rows, (int)d, nullptr, nullptr, S(stream)),
+                      "iw_layernorm32");
+}
+
+int iw_layernorm32_stats(const int16_t *x, int32_t *mean, int32_t *variance, int32_t *renorm_shift, int64_t rows,
+                         int64_t d, void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    return cuda_check(iw::layernorm32_stats(x, (int)rows, (int)d, mean, variance, renorm_shift, S(stream)),
+                      "iw_layernorm32_stats");
+}
+
+__global__ void any_negative_kernel(const int32_t *x, int64_t n, int *flag) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        if (x[i] < 0) atomicExch(flag, 1);
+}
+
+static int check_nonnegative(const int32_t *x, int64_t n, cudaStream_t st, const char *name, const char *msg) {
+    if (n <= 0) return IW_OK;
+    Scratch f(st);
+    if (int r = cuda_check(f.alloc(sizeof(int)), name)) return r;
+    if (int r = cuda_check(cudaMemsetAsync(f.p, 0, sizeof(int), st), name)) return r;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 1024) blocks = 1024;
+    any_negative_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, n, (int *)f.p);
+    int h = 0;
+    if (int r = cuda_check(cudaMemcpyAsync(&h, f.p, sizeof(int), cudaMemcpyDeviceToHost, st), name)) return r;
+    if (int r = cuda_check(cudaStreamSynchronize(st), name)) return r;
+    if (h) return fail(IW_EVALUE, "%s", msg);
+    return IW_OK;
+}
+
+int iw_layernorm32_rsqrt(const int32_t *variance, int32_t *invstd, int64_t numel, void *stream) {
+    if (int r = check_nonnegative(variance, numel, S(stream), "iw_layernorm32_rsqrt", "input must be non-negative"))
+        return r;
+    return cuda_check(iw::fisr_vec(variance, invstd, numel, 13u, S(stream)), "iw_layernorm32_rsqrt");
+}
+
+int iw_gelu(const int8_t *x, const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,
+            const uint8_t *luto_multiplier, const int8_t *luto_shift, int8_t *y, int64_t numel, int64_t channels,
+            int64_t luti_count, int64_t luto_count, void *stream) {
+    if (channels <= 0 && numel > 0) return fail(IW_EINVAL, "iw_gelu: input must have at least one dimension");
+    if (!(luti_count == 1 || luti_count == channels))
+        return fail(IW_EINVAL, "luti parameters must be scalar or match input.size(-1)");
+    if (!(luto_count == 1 || luto_count == channels))
+        return fail(IW_EINVAL, "luto parameters must be scalar or match input.size(-1)");
+    iw::GeluParams g{lut, luti_multiplier, luti_shift, luto_multiplier, luto_shift, (int)luti_count, (int)luto_count};
+    return cuda_check(iw::gelu(x, y, numel, (int)channels, g, S(stream)), "iw_gelu");
+}
+
+int iw_qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, uint8_t multiplier, int8_t shift,
+                         int16_t *qk, int16_t *row_max_plus1, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                         int64_t D, void *stream) {
+    if (B < 0 || H < 0 || Tq < 0 || Tk < 0 || D < 0) return fail(IW_EINVAL, "iw_qk_requant_rowmax: invalid shape");
+    return cuda_check(iw::qk_requant_rowmax(q, k, mask, qk, row_max_plus1, (int)B, (int)H, (int)Tq, (int)Tk, (int)D,
+                                            multiplier, (int32_t)shift, S(stream)),
+                      "iw_qk_requant_rowmax");
+}
+
+int iw_shift_exp(const int16_t *x, const int16_t *row_max_plus1, const uint8_t *mask, int32_t frac_bits, uint8_t *p,
+                 int32_t *row_sum, int64_t B, int64_t H, int64_t Tq, int64_t Tk, void *stream) {
+    if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    return cuda_check(iw::shift_exp(x, row_max_plus1, mask, p, row_sum, (int)B, (int)H, (int)Tq, (int)Tk, frac_bits,
+                                    S(stream)),
+                      "iw_shift_exp");
+}
+
+int iw_pv_norm_requant(const uint8_t *p, const int8_t *v, const int32_t *row_sum, uint8_t av_multiplier,
+                       int8_t av_shift, int64_t rsqrt_offset, int8_t *y, int64_t B, int64_t H, int64_t Tq,
+                       int64_t Tk, int64_t D, void *stream) {
+    if (!(rsqrt_offset >= 0 && rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
+    cudaStream_t st = S(stream);
+    if (int r = check_nonnegative(row_sum, B * H * Tq, st, "iw_pv_norm_requant", "row_sum must be non-negative"))
+        return r;
+    Scratch bad(st);
+    if (int r = cuda_check(bad.alloc(sizeof(int)), "iw_pv_norm_requant")) return r;
+    if (int r = cuda_check(cudaMemsetAsync(bad.p, 0, sizeof(int), st), "iw_pv_norm_requant")) return r;
+    return cuda_check(iw::pv_norm_requant(p, v, row_sum, av_multiplier, av_shift, (uint32_t)rsqrt_offset, y, (int)B,
+                                          (int)H, (int)Tq, (int)Tk, (int)D, (int *)bad.p, st),
+                      "iw_pv_norm_requant");
+}
+
+int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, int64_t ldk, int64_t k_bs,
+                 const int8_t *v, int64_t ldv, int64_t v_bs, int8_t *y, int64_t ldy, int64_t y_bs, int64_t B,
+                 int64_t H, int64_t Tq, int64_t Tk, int mask_mode, const uint8_t *mask, uint8_t qk_multiplier,
+                 int8_t qk_shift, int32_t frac_bits, uint8_t av_multiplier, int8_t av_shift, int64_t rsqrt_offset,
+                 void *stream) {
+    if (B < 0 || H < 0 || Tq < 0 || Tk < 0) return fail(IW_EINVAL, "iw_attention: invalid shape");
+    if (Tq > Tk && mask_mode == 1) return fail(IW_EINVAL, "iw_attention: causal mask needs Tq <= Tk");
+    if (mask_mode == 2 && !mask) return fail(IW_EINVAL, "iw_attention: mask_mode 2 needs a mask");
+    if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    if (!(rsqrt_offset >= 0 && rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
+    if ((ldq | ldk | ldv | q_bs | k_bs | v_bs) & 15 || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15 ||
+        (reinterpret_cast<uintptr_t>(v) & 1))
+        return fail(IW_EINVAL, "iw_attention: Q/K rows must be 16-byte aligned");
+    iw::AttnArgs a;
+    a.q = q; a.ldq = ldq; a.q_bs = q_bs;
+    a.k = k; a.ldk = ldk; a.k_bs = k_bs;
+    a.v = v; a.ldv = ldv; a.v_bs = v_bs;
+    a.out = y; a.ldo = ldy; a.o_bs = y_bs;
+    a.Tq = (int)Tq; a.Tk = (int)Tk; a.Tk_dev = nullptr; a.Tk_cap = (int)Tk;
+    a.mask_mode = mask_mode; a.mask = mask;
+    a.qk_mult = qk_multiplier; a.qk_shift = qk_shift; a.frac_bits = frac_bits;
+    a.av_mult = av_multiplier; a.av_shift = av_shift; a.rsqrt_offset = (uint32_t)rsqrt_offset;
+    return cuda_check(iw::attention_cc(a, (int)B, (int)H, S(stream)), "iw_attention");
+}
+
+int iw_conv1d(const int8_t *x, const int8_t *weight, const int32_t *bias, uint32_t multiplier, int8_t shift,
+              int64_t stride, int64_t padding, int8_t *y, int64_t B, int64_t Cin, int64_t Tin, int64_t Cout,
+              int64_t K, void *stream) {
+    if (stride <= 0) return fail(IW_EINVAL, "stride must be positive");
+    if (padding < 0) return fail(IW_EINVAL, "padding must be non-negative");
+    if (Cin <= 0) return fail(IW_EINVAL, "input channel count must be positive");
+    if (Tin <= 0) return fail(IW_EINVAL, "input length must be positive");
+    if (Cout <= 0) return fail(IW_EINVAL, "output channel count must be positive");
+    if (K <= 0) return fail(IW_EINVAL, "kernel size must be positive");
+    const int64_t num = Tin + 2 * padding - K;
+    if (num < 0) return fail(IW_EINVAL, "invalid Conv1d geometry: output length would be non-positive");
+    const int64_t Tout = num / stride + 1;
+    if (B == 0) return IW_OK;
+    cudaStream_t st = S(stream);
+    const int64_t Kg = Cin * K, Kp = round_up(Kg, 16);
+    const int64_t M = B * Tout;
+    Scratch cols(st), ws(st);
+    if (int r = cuda_check(cols.alloc((size_t)M * Kp), "iw_conv1d")) return r;
+    if (int r = cuda_check(iw::im2col(x, (int8_t *)cols.p, (int)B, (int)Cin, (int)Tin, (int)K, (int)stride,
+                                      (int)padding, (int)Tout, Kp, 0, st),
+                           "iw_conv1d"))
+        return r;
+    const int8_t *wg = weight;
+    if (Kp != Kg || (reinterpret_cast<uintptr_t>(weight) & 15)) {
+        if (int r = cuda_check(ws.alloc((size_t)Cout * Kp), "iw_conv1d")) return r;
+        if (int r = cuda_check(iw::pad_rows(weight, Cout, Kg, (int8_t *)ws.p, Kp, st), "iw_conv1d")) return r;
+        wg = (const int8_t *)ws.p;
+    }
+    iw::EpiParams p;
+    p.out = y;
+    p.ldo = Cout;
+    p.bias = bias;
+    p.per_channel = 0;
+    p.smult = multiplier;
+    p.sshift = (uint32_t)(shift > 0 ? shift : 0);
+    p.transpose_T = (int)Tout;
+    iw::GemmShape g{(const int8_t *)cols.p, Kp, wg, Kp, (int)M, (int)Cout, (int)Kp};
+    return cuda_check(iw::gemm_i8_launch(g, iw::EPI_L8, p, st), "iw_conv1d");
+}
+
+int iw_add_requant15(const int8_t *x, const int8_t *addend, const uint16_t *multiplier, const int8_t *shift,
+                     int16_t *y, int64_t B, int64_t T, int64_t C, int64_t multiplier_count, int64_t shift_count,
+                     void *stream) {
+    if (!(multiplier_count == 1 || multiplier_count == C)) return fail(IW_EINVAL, "multiplier must contain 1 or C elements");
+    if (!(shift_count == 1 || shift_count == C)) return fail(IW_EINVAL, "shift must contain 1 or C elements");
+    return cuda_check(iw::add_requant15(x, nullptr, addend, multiplier, shift, y, (int)B, (int)T, (int)C,
+                                        (int)multiplier_count, (int)shift_count, 0, nullptr, S(stream)),
+                      "iw_add_requant15");
+}
+
+int iw_embed_add_requant15(const int8_t *table, const int64_t *tokens, const int8_t *pe, int64_t offset,
+                           const uint16_t *multiplier, const int8_t *shift, int16_t *y, int64_t B, int64_t T,
+                           int64_t C, int64_t multiplier_count, int64_t shift_count, void *stream) {
+    if (!(multiplier_count == 1 || multiplier_count == C)) return fail(IW_EINVAL, "multiplier must contain 1 or C elements");
+    if (!(shift_count == 1 || shift_count == C)) return fail(IW_EINVAL, "shift must contain 1 or C elements");
+    if (offset < 0) return fail(IW_EINVAL, "iw_embed_add_requant15: negative offset");
+    return cuda_check(iw::add_requant15(table, tokens, pe, multiplier, shift, y, (int)B, (int)T, (int)C,
+                                        (int)multiplier_count, (int)shift_count, (int)offset, nullptr, S(stream)),
+                      "iw_embed_add_requant15");
+}
+
+int iw_classifier(const int8_t *x, const int8_t *weight, uint32_t multiplier, int8_t shift, int8_t *y, int64_t M,
+                  int64_t K, int64_t N, void *stream) {
+    if (K <= 0) return fail(IW_EINVAL, "hidden size must be positive");
+    if (N <= 0) return fail(IW_EINVAL, "vocabulary size must be positive");
+    if (M == 0) return IW_OK;
+    cudaStream_t st = S(stream);
+    Scratch xs(st), ws(st);
+    const int8_t *xg = x, *wg = weight;
+    int64_t Kp = K;
+    if (K % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(weight) & 15)) {
+        Kp = round_up(K, 16);
+        if (int r = cuda_check(xs.alloc((size_t)M * Kp), "iw_classifier")) return r;
+        if (int r = cuda_check(ws.alloc((size_t)N * Kp), "iw_classifier")) return r;
+        if (int r = cuda_check(iw::pad_rows(x, M, K, (int8_t *)xs.p, Kp, st), "iw_classifier")) return r;
+        if (int r = cuda_check(iw::pad_rows(weight, N, K, (int8_t *)ws.p, Kp, st), "iw_classifier")) return r;
+        xg = (const int8_t *)xs.p;
+        wg = (const int8_t *)ws.p;
+    }
+    iw::EpiParams p;
+    p.out = y;
+    p.ldo = N;
+    p.per_channel = 0;
+    p.smult = multiplier;
+    p.sshift = (uint32_t)(shift > 0 ? shift : 0);
+    iw::GemmShape g{xg, Kp, wg, Kp, (int)M, (int)N, (int)Kp};
+    return cuda_check(iw::gemm_i8_launch(g, iw::EPI_L8, p, st), "iw_classifier");
+}
+
+int iw_rowsum_i8(const int8_t *x, int64_t ldx, int64_t M, int64_t K, int32_t *y, void *stream) {
+    return cuda_check(iw::rowsum_i8(x, ldx, (int)M, (int)K, y, S(stream)), "iw_rowsum_i8");
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// gemm_i8.cuh -- host-visible description of the tcgen05 w8a8 GEMM and its
+// fused epilogues.
+//
+// Y[m, n] = epilogue( sum_k X[m, k] * W[n, k] )   X: [M, K] int8 row-major,
+//                                                W: [N, K] int8 row-major.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace iw {
+
+enum EpiMode : int {
+    EPI_ACC32 = 0,    // int32 out: acc + bias - wz*rowsum            (linear8_accum)
+    EPI_L8 = 1,       // int8 out: Linear8 / conv / classifier requant (+GeLU, +pos-add)
+    EPI_L32 = 2,      // int32 out: Linear32 requant (mulh, wrapping left shift)
+    EPI_L32_RES = 3,  // int16 out: Linear32 requant fused with Residual15
+};
+
+struct EpiParams {
+    void *out = nullptr;
+    int64_t ldo = 0;  // output row stride in elements
+    // zero point / bias (Linear8/32, linear.py:50-97)
+    const int32_t *bias = nullptr;    // [N]
+    const int8_t *wz = nullptr;       // [N] weight zero points
+    const int32_t *rowsum = nullptr;  // [M] sum of each X row (needed with wz)
+    // requant: per channel (Linear8/32) or one scalar (conv, classifier)
+    const uint32_t *mult = nullptr;   // [N]
+    const int8_t *shift = nullptr;    // [N]
+    int per_channel = 1;
+    uint32_t smult = 0;   // scalar multiplier
+    uint32_t sshift = 0;  // scalar shift, already max(s,0)
+    // fused GeLU on the int8 result (gelu_scalar.cpp)
+    int gelu = 0;
+    const uint8_t *lut = nullptr;
+    const uint8_t *gmi = nullptr;
+    const int8_t *gsi = nullptr;
+    const uint8_t *gmo = nullptr;
+    const int8_t *gso = nullptr;
+    int gelu_in_pc = 0, gelu_out_pc = 0;  // per-channel (1) or per-tensor (0)
+    // fused Residual15 (EPI_L32_RES)
+    const int16_t *res = nullptr;
+    int64_t ldr = 0;
+    uint32_t res_mult = 0;
+    // fused positional add + requant to INT15 (add_requant15_scalar.cpp)
+    int posadd = 0;
+    const int8_t *pe = nullptr;  // [T, N]
+    int pe_T = 1;                // rows m map to position m % pe_T
+    const uint16_t *pm = nullptr;
+    const int8_t *ps = nullptr;
+    int pos_pc = 1;
+    // optional: int8 output written as [B, N, T] with m = b*T + t
+    int transpose_T = 0;
+    // optional: per-head transposed store for attention V^T:
+    // out[(b*H + h)*D + d][t] with m = b*T + t, n = h*D + d, row stride ldo
+    int vt_T = 0, vt_D = 0;
+    // optional: accumulate per-row sums of the int8 output (next GEMM's
+    // zero-point term)
+    int32_t *rowsum_out = nullptr;
+};
+
+struct GemmShape {
+    const int8_t *x;
+    int64_t ldx;  // row stride of X in bytes (multiple of 16)
+    const int8_t *w;
+    int64_t ldw;  // row stride of W in bytes (multiple of 16)
+    int M, N, K;
+};
+
+// Launches the tcgen05 GEMM with the given epilogue on `stream`.
+// Returns a cudaError_t (cudaSuccess when the launch was queued).
+cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p, cudaStream_t stream,
+                           int bn_hint = 0);
+
+// Number of SMs of the current device (cached).
+int num_sms();
+
+}  // namespace iw

@@ -1,0 +1,135 @@
+// iw_common.cuh -- integer fixed-point arithmetic shared by every kernel.
+//
+// Device restatements of the reference primitives in
+// i_whisper/kernels/csrc/common/fixedpoint.h (vcsd-lab/I-Whisper). All
+// wrap-around behaviour is spelled out with uint32 arithmetic.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define IW_DEV __device__ __forceinline__
+
+namespace iw {
+
+IW_DEV int32_t wadd(int32_t a, int32_t b) { return (int32_t)((uint32_t)a + (uint32_t)b); }
+IW_DEV int32_t wsub(int32_t a, int32_t b) { return (int32_t)((uint32_t)a - (uint32_t)b); }
+IW_DEV int32_t wmul(int32_t a, int32_t b) { return (int32_t)((uint32_t)a * (uint32_t)b); }
+__host__ __device__ __forceinline__ int32_t clampi(int32_t v, int32_t lo, int32_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// fixedpoint.h:35-44: high word of (int64)x * (uint32)m. Written as the
+// unsigned high product corrected for a negative x:
+//   (int64)x*m = (uint32)x*m - (x<0 ? m<<32 : 0)
+IW_DEV int32_t mulh(int32_t x, uint32_t m) {
+    uint32_t hi = __umulhi((uint32_t)x, m);
+    return (int32_t)(hi - (x < 0 ? m : 0u));
+}
+
+// fixedpoint.h:47-87: shift 0 -> x, shift >= 32 -> 0, else
+// (x + 2^(s-1) - signbit) with uint32 wrap, arithmetic shift right.
+IW_DEV int32_t rrs(int32_t x, uint32_t s) {
+    if (s == 0) return x;
+    if (s >= 32) return 0;
+    uint32_t v = (uint32_t)x + (1u << (s - 1)) - ((uint32_t)x >> 31);
+    return ((int32_t)v) >> s;
+}
+
+// Same as rrs for a shift known to lie in [1,31].
+IW_DEV int32_t rrs_pos(int32_t x, uint32_t s) {
+    uint32_t v = (uint32_t)x + (1u << (s - 1)) - ((uint32_t)x >> 31);
+    return ((int32_t)v) >> s;
+}
+
+IW_DEV int32_t bit_length_nonneg(int32_t x) { return x == 0 ? 0 : 32 - __clz(x); }
+
+// layernorm_scalar.cpp:309-343 -- int32 -> fp32 bit pattern with the
+// mantissa truncated (never rounded).
+IW_DEV int32_t int32_to_fp32_bits_trunc(int32_t x) {
+    if (x == 0) return 0;
+    int32_t e = 31 - __clz(x);
+    uint32_t ux = (uint32_t)x;
+    uint32_t sig = e <= 23 ? (ux << (23 - e)) : (ux >> (e - 23));
+    return (int32_t)(((uint32_t)(e + 127) << 23) | (sig & 0x007FFFFFu));
+}
+
+// layernorm_scalar.cpp:345-381 -- fp32 bit pattern -> int32, truncating;
+// a left shift of the 24-bit significand keeps only its low 32 bits.
+IW_DEV int32_t fp32_bits_to_int32_trunc(int32_t bits) {
+    uint32_t raw = (uint32_t)bits;
+    int32_t e = (int32_t)((raw >> 23) & 0xFFu) - 127;
+    uint64_t sig = (uint64_t)((1u << 23) | (raw & 0x007FFFFFu));
+    if (e < 0) return 0;
+    uint64_t v;
+    if (e >= 23) {
+        int32_t sh = e - 23;
+        v = sh >= 64 ? 0ull : (sig << sh);
+    } else {
+        v = sig >> (23 - e);
+    }
+    return (int32_t)(uint32_t)v;
+}
+
+// layernorm_scalar.cpp:383-437 -- integer fast inverse square root in
+// Q(off): magic-constant seed computed on the truncated fp32 bit pattern,
+// then two Newton steps with wrapping products and rounding shifts.
+IW_DEV int32_t fisr(int32_t x, uint32_t off) {
+    int32_t i = int32_to_fp32_bits_trunc(x);
+    i = (int32_t)0x5f3759dfu - (i >> 1);
+    int32_t y = fp32_bits_to_int32_trunc((int32_t)((uint32_t)i + (off << 23)));
+    const int32_t three = (int32_t)(3u << off);
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        int32_t xys = rrs(wmul(x, y), off);
+        int32_t t = wmul(xys, y);
+        y = rrs(wmul(y, wsub(three, t)), off + 1);
+    }
+    return y;
+}
+
+// gelu_scalar.cpp:10-181 -- one element of the LUT GeLU.
+IW_DEV int32_t gelu_one(int32_t x, const uint8_t *lut, uint32_t mi, uint32_t si,
+                        uint32_t mo, uint32_t so) {
+    int32_t idx = rrs(x * (int32_t)mi, si);
+    idx = clampi(idx + 8, 0, 15);
+    int32_t v = x * (int32_t)lut[idx];
+    v = v * (int32_t)mo;
+    v = rrs(v, so);
+    return clampi(v, -127, 127);
+}
+
+// attention_scalar.cpp:388-560 -- shift-based exp2 of (x - rowmax1) in
+// int16 wrapping arithmetic. The caller handles masked lanes.
+IW_DEV int32_t shift_exp_one(int32_t x, int32_t xm, int32_t fb) {
+    int16_t xs = (int16_t)(x - xm);
+    if (xs > 0) return 0;
+    int16_t half = (int16_t)(xs >> 1);
+    int16_t six = (int16_t)(xs >> 4);
+    int16_t fix = (int16_t)((int16_t)(xs + half) - six);
+    int16_t xi = (int16_t)(fix >> fb);
+    int32_t scale = 1 << fb;
+    int16_t ip = (int16_t)((int32_t)xi * scale);
+    int16_t fr = (int16_t)(fix - ip);
+    int16_t num = (int16_t)(scale + (int32_t)(fr >> 1));
+    int16_t e;
+    if (xi > 0) {
+        e = 0;
+    } else {
+        int32_t es = -(int32_t)xi;
+        e = es >= 16 ? (int16_t)0 : (int16_t)(num >> es);
+    }
+    if (fb > 7) return (int32_t)(uint8_t)((int32_t)e >> (fb - 7));
+    return (int32_t)(uint8_t)e;
+}
+
+// Device-side status word: set by bounded waits that gave up, read by the
+// host after a synchronisation (iw_device_status in the C ABI).
+enum : uint32_t {
+    IW_DEVERR_NONE = 0,
+    IW_DEVERR_WAIT_TIMEOUT = 1u << 0,
+};
+
+// The library is built as one translation unit (iw_lib.cu), so this single
+// definition is shared by every kernel.
+__device__ uint32_t g_device_status = 0;
+
+}  // namespace iw

@@ -1,0 +1,650 @@
+// kernels.cu -- bandwidth-bound kernels of the integer path: row sums,
+// LayerNorm32, GeLU, Residual15, Add+Requant15 / embedding gather, im2col
+// for the conv stem, the CUDA-core attention used for decode-shaped
+// problems, and the reference-layout attention stages.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "iw_common.cuh"
+#include "kernels.cuh"
+
+namespace iw {
+
+// ---------------------------------------------------------------------------
+// Row sums of an int8 matrix (zero-point term of Linear8/32, linear.py:89-91)
+// ---------------------------------------------------------------------------
+__global__ void rowsum_i8_kernel(const int8_t *__restrict__ x, int64_t ldx, int M, int K, int32_t *__restrict__ out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const int8_t *r = x + (int64_t)warp * ldx;
+    int32_t s = 0;
+    if ((K & 3) == 0 && (reinterpret_cast<uintptr_t>(r) & 3) == 0) {
+        const int32_t *r4 = reinterpret_cast<const int32_t *>(r);
+        for (int i = lane; i < K / 4; i += 32) s += __dp4a(r4[i], 0x01010101, 0);
+    } else {
+        for (int i = lane; i < K; i += 32) s += r[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) out[warp] = s;
+}
+
+cudaError_t rowsum_i8(const int8_t *x, int64_t ldx, int M, int K, int32_t *out, cudaStream_t st) {
+    if (M <= 0) return cudaSuccess;
+    const int threads = 256;
+    const int blocks = (M * 32 + threads - 1) / threads;
+    rowsum_i8_kernel<<<blocks, threads, 0, st>>>(x, ldx, M, K, out);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm32 (layernorm_scalar.cpp:464-624). One warp per row; the row
+// lives in registers (D/128 groups of 4 int16 per lane).
+// ---------------------------------------------------------------------------
+template <int D>
+IW_DEV int32_t norm_reduce(int32_t x) {
+    // layernorm_scalar.cpp:14-56
+    if constexpr (D == 384) return (x + (x >> 2) + (x >> 3)) >> 9;
+    else if constexpr (D == 512) return x >> 9;
+    else if constexpr (D == 768) return (x + (x >> 2) + (x >> 3)) >> 10;
+    else if constexpr (D == 1024) return x >> 10;
+    else return (x + (x >> 1)) >> 11;  // 1280
+}
+
+IW_DEV int32_t warp_sum(int32_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+IW_DEV int32_t warp_max(int32_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) layernorm32_kernel(const int16_t *__restrict__ x, int64_t ldx,
+                                                           const int8_t *__restrict__ gamma,
+                                                           const int32_t *__restrict__ beta, LnParams p,
+                                                           int8_t *__restrict__ y, int64_t ldy, int rows,
+                                                           int32_t *__restrict__ rowsum_out,
+                                                           int32_t *__restrict__ rowsum_zero) {
+    constexpr int G = D / 128;  // groups of 4 elements per lane
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int16_t *xr = x + (int64_t)row * ldx;
+    int32_t v[G * 4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(xr + (g * 32 + lane) * 4);
+        v[4 * g + 0] = (int16_t)(u.x & 0xFFFF);
+        v[4 * g + 1] = (int16_t)(u.x >> 16);
+        v[4 * g + 2] = (int16_t)(u.y & 0xFFFF);
+        v[4 * g + 3] = (int16_t)(u.y >> 16);
+    }
+    int32_t s = 0;
+#pragma unroll
+    for (int i = 0; i < G * 4; ++i) s += v[i];
+    s = warp_sum(s);
+    const int32_t mean = norm_reduce<D>(s);
+    int32_t mx = 0;
+#pragma unroll
+    for (int i = 0; i < G * 4; ++i) {
+        v[i] -= mean;
+        mx = max(mx, wmul(v[i], v[i]));
+    }
+    mx = warp_max(mx);
+    int32_t rs = bit_length_nonneg(mx) - 16;
+    rs = rs < 0 ? 0 : rs;
+    rs = (rs + 1) & ~1;
+    int32_t vs = 0;
+#pragma unroll
+    for (int i = 0; i < G * 4; ++i) vs = wadd(vs, rrs(wmul(v[i], v[i]), (uint32_t)rs));
+    vs = warp_sum(vs);
+    const int32_t var = norm_reduce<D>(vs);
+    const int32_t inv = fisr(var, p.rsqrt_offset);
+    const uint32_t nshift = (uint32_t)(p.ln_shift + (rs >> 1));
+    int32_t osum = 0;
+    int8_t *yr = y + (int64_t)row * ldy;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int c0 = (g * 32 + lane) * 4;
+        const char4 gm = *reinterpret_cast<const char4 *>(gamma + c0);
+        const int8_t gg[4] = {gm.x, gm.y, gm.z, gm.w};
+        int4 bb = make_int4(0, 0, 0, 0);
+        if (beta) bb = *reinterpret_cast<const int4 *>(beta + c0);
+        const int32_t be[4] = {bb.x, bb.y, bb.z, bb.w};
+        uint32_t packed = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            int32_t t = wmul(v[4 * g + u], inv);
+            t = wmul(t, p.ln_mult);
+            t = rrs(t, nshift);
+            t = clampi(t, -16383, 16383);
+            t = wmul(t, (int32_t)gg[u]);
+            t = wadd(t, be[u]);
+            t = mulh(t, p.out_mult);
+            t = rrs(t, p.out_shift);
+            t = clampi(t, -127, 127);
+            osum += t;
+            packed |= (uint32_t)(uint8_t)t << (8 * u);
+        }
+        *reinterpret_cast<uint32_t *>(yr + c0) = packed;
+    }
+    if (rowsum_out) {
+        osum = warp_sum(osum);
+        if (lane == 0) rowsum_out[row] = osum;
+    }
+    if (rowsum_zero && lane == 0) rowsum_zero[row] = 0;
+}
+
+cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, const int32_t *beta, const LnParams &p,
+                        int8_t *y, int64_t ldy, int rows, int d, int32_t *rowsum_out, int32_t *rowsum_zero,
+                        cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    if ((reinterpret_cast<uintptr_t>(x) & 7) || (ldx & 3) || (reinterpret_cast<uintptr_t>(y) & 3) || (ldy & 3) ||
+        (reinterpret_cast<uintptr_t>(gamma) & 3) || (beta && (reinterpret_cast<uintptr_t>(beta) & 15)))
+        return cudaErrorMisalignedAddress;
+    const int threads = 256;
+    const int blocks = (rows * 32 + threads - 1) / threads;
+#define IW_LN_CASE(DD)                                                                                        \
+    case DD:                                                                                                  \
+        layernorm32_kernel<DD><<<blocks, threads, 0, st>>>(x, ldx, gamma, beta, p, y, ldy, rows, rowsum_out, \
+                                                            rowsum_zero);                                     \
+        break;
+    switch (d) {
+        IW_LN_CASE(384)
+        IW_LN_CASE(512)
+        IW_LN_CASE(768)
+        IW_LN_CASE(1024)
+        IW_LN_CASE(1280)
+    default: return cudaErrorInvalidValue;
+    }
+#undef IW_LN_CASE
+    return cudaGetLastError();
+}
+
+// LayerNorm statistics only (layernorm32_stats_scalar): mean, variance,
+// renorm shift per row. Any width the reference accepts.
+__global__ void ln_stats_kernel(const int16_t *__restrict__ x, int rows, int d, int32_t *mean_o, int32_t *var_o,
+                                int32_t *rs_o) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int16_t *xr = x + (int64_t)row * d;
+    int32_t s = 0;
+    for (int c = lane; c < d; c += 32) s += xr[c];
+    s = warp_sum(s);
+    int32_t mean;
+    switch (d) {
+    case 384: mean = norm_reduce<384>(s); break;
+    case 512: mean = norm_reduce<512>(s); break;
+    case 768: mean = norm_reduce<768>(s); break;
+    case 1024: mean = norm_reduce<1024>(s); break;
+    default: mean = norm_reduce<1280>(s); break;
+    }
+    int32_t mx = 0;
+    for (int c = lane; c < d; c += 32) {
+        int32_t ce = (int32_t)xr[c] - mean;
+        mx = max(mx, wmul(ce, ce));
+    }
+    mx = warp_max(mx);
+    int32_t rs = bit_length_nonneg(mx) - 16;
+    rs = rs < 0 ? 0 : rs;
+    rs = (rs + 1) & ~1;
+    int32_t vs = 0;
+    for (int c = lane; c < d; c += 32) {
+        int32_t ce = (int32_t)xr[c] - mean;
+        vs = wadd(vs, rrs(wmul(ce, ce), (uint32_t)rs));
+    }
+    vs = warp_sum(vs);
+    int32_t var;
+    switch (d) {
+    case 384: var = norm_reduce<384>(vs); break;
+    case 512: var = norm_reduce<512>(vs); break;
+    case 768: var = norm_reduce<768>(vs); break;
+    case 1024: var = norm_reduce<1024>(vs); break;
+    default: var = norm_reduce<1280>(vs); break;
+    }
+    if (lane == 0) {
+        mean_o[row] = mean;
+        var_o[row] = var;
+        rs_o[row] = rs;
+    }
+}
+
+cudaError_t layernorm32_stats(const int16_t *x, int rows, int d, int32_t *mean, int32_t *var, int32_t *rs,
+                              cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    ln_stats_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, rows, d, mean, var, rs);
+    return cudaGetLastError();
+}
+
+__global__ void fisr_kernel(const int32_t *x, int32_t *y, int64_t n, uint32_t off) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = fisr(x[i], off);
+}
+
+cudaError_t fisr_vec(const int32_t *x, int32_t *y, int64_t n, uint32_t off, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    fisr_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n, off);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// GeLU (gelu_scalar.cpp:10-181), standalone.
+// ---------------------------------------------------------------------------
+__global__ void gelu_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, int64_t n, int channels,
+                            GeluParams g) {
+    __shared__ uint8_t lut[16];
+    if (threadIdx.x < 16) lut[threadIdx.x] = g.lut[threadIdx.x];
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % channels);
+        const int a = g.n_in == 1 ? 0 : c;
+        const int b = g.n_out == 1 ? 0 : c;
+        y[i] = (int8_t)gelu_one(x[i], lut, g.mi[a], (uint32_t)clampi(g.si[a], 0, 32), g.mo[b],
+                                (uint32_t)clampi(g.so[b], 0, 32));
+    }
+}
+
+cudaError_t gelu(const int8_t *x, int8_t *y, int64_t n, int channels, const GeluParams &g, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    gelu_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, y, n, channels, g);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Residual15 (residual15_scalar.cpp:9-27), standalone.
+// ---------------------------------------------------------------------------
+__global__ void residual15_kernel(const int32_t *__restrict__ br, const int16_t *__restrict__ r, uint32_t m,
+                                  int16_t *__restrict__ y, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int32_t b = wadd(br[i], wmul((int32_t)r[i], (int32_t)m));
+        y[i] = (int16_t)clampi(rrs_pos(b, 15), -16383, 16383);
+    }
+}
+
+cudaError_t residual15(const int32_t *br, const int16_t *r, uint16_t m, int16_t *y, int64_t n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    residual15_kernel<<<(unsigned)blocks, 256, 0, st>>>(br, r, m, y, n);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Add + requant to INT15 (add_requant15_scalar.cpp:29-80). With `tokens`
+// set, the int8 input row is gathered from the embedding table
+// (TextDecoder_int.forward, model_int.py:1411-1428) and the addend row is
+// pe[offset + t]; `offset_dev` (optional) supplies the offset from device
+// memory so the launch can be replayed by a CUDA graph.
+// ---------------------------------------------------------------------------
+__global__ void add_requant15_kernel(const int8_t *__restrict__ x, const int64_t *__restrict__ tokens,
+                                     const int8_t *__restrict__ addend, const uint16_t *__restrict__ mult,
+                                     const int8_t *__restrict__ shift, int16_t *__restrict__ y, int B, int T, int C,
+                                     int n_mult, int n_shift, int offset, const int32_t *offset_dev) {
+    const int64_t total = (int64_t)B * T * C;
+    const int off = offset_dev ? *offset_dev : offset;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % C);
+        const int64_t bt = i / C;
+        const int t = (int)(bt % T);
+        int32_t xv;
+        if (tokens) xv = x[tokens[bt] * C + c];
+        else xv = x[i];
+        int32_t v = xv + (int32_t)addend[(int64_t)(off + t) * C + c];
+        v = wmul(v, (int32_t)mult[n_mult == 1 ? 0 : c]);
+        const int32_t s = shift[n_shift == 1 ? 0 : c];
+        v = rrs(v, (uint32_t)(s > 0 ? s : 0));
+        y[i] = (int16_t)clampi(v, -16383, 16383);
+    }
+}
+
+cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *addend, const uint16_t *mult,
+                          const int8_t *shift, int16_t *y, int B, int T, int C, int n_mult, int n_shift, int offset,
+                          const int32_t *offset_dev, cudaStream_t st) {
+    const int64_t total = (int64_t)B * T * C;
+    if (total <= 0) return cudaSuccess;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    add_requant15_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, tokens, addend, mult, shift, y, B, T, C, n_mult, n_shift,
+                                                           offset, offset_dev);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// im2col for the conv stem (conv1d_scalar.cpp:42-104 ordering: column
+// cin*K + k holds x[cin, t*stride - pad + k], zero outside [0, Tin)).
+// `channels_last` selects an input stored [B, Tin, Cin] instead of
+// [B, Cin, Tin]. The output row stride `ldo` may exceed Cin*K (zero pad).
+// ---------------------------------------------------------------------------
+__global__ void im2col_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ out, int B, int Cin, int Tin, int K,
+                              int stride, int pad, int Tout, int64_t ldo, int channels_last) {
+    const int64_t cols = ldo;
+    const int64_t total = (int64_t)B * Tout * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t col = i % cols;
+        const int64_t bt = i / cols;
+        const int t = (int)(bt % Tout);
+        const int b = (int)(bt / Tout);
+        int8_t v = 0;
+        if (col < (int64_t)Cin * K) {
+            const int c = (int)(col / K), k = (int)(col % K);
+            const int pos = t * stride - pad + k;
+            if (pos >= 0 && pos < Tin)
+                v = channels_last ? x[((int64_t)b * Tin + pos) * Cin + c] : x[((int64_t)b * Cin + c) * Tin + pos];
+        }
+        out[i] = v;
+    }
+}
+
+cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K, int stride, int pad, int Tout,
+                   int64_t ldo, int channels_last, cudaStream_t st) {
+    const int64_t total = (int64_t)B * Tout * ldo;
+    if (total <= 0) return cudaSuccess;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 16384) blocks = 16384;
+    im2col_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, out, B, Cin, Tin, K, stride, pad, Tout, ldo, channels_last);
+    return cudaGetLastError();
+}
+
+// 2-D copy into a zero-padded buffer (row stride ldo >= cols).
+__global__ void pad_rows_kernel(const int8_t *__restrict__ x, int64_t rows, int64_t cols, int8_t *__restrict__ out,
+                                int64_t ldo) {
+    const int64_t total = rows * ldo;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / ldo, c = i % ldo;
+        out[i] = c < cols ? x[r * cols + c] : (int8_t)0;
+    }
+}
+
+cudaError_t pad_rows(const int8_t *x, int64_t rows, int64_t cols, int8_t *out, int64_t ldo, cudaStream_t st) {
+    const int64_t total = rows * ldo;
+    if (total <= 0) return cudaSuccess;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 16384) blocks = 16384;
+    pad_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, rows, cols, out, ldo);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Fused integer attention on CUDA cores (MultiHeadAttention_int.qkv_attention,
+// model_int.py:774-1042; attention_scalar.cpp:216-813), head_dim 64.
+// One CTA handles QB query rows of one (batch, head): QK^T + requant +
+// row max (scores kept in shared memory), shift-exp + row sum, P.V,
+// FISR^2 normalisation and the AV requant, written to [B, Tq, H*64].
+// Used for decode-shaped problems (few query rows) where the K/V stream
+// from HBM dominates.
+// ---------------------------------------------------------------------------
+static constexpr int kAttnThreads = 256;
+static constexpr int kAttnQB = 4;
+
+__global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
+    extern __shared__ uint8_t smem[];
+    const int Tk = a.Tk_dev ? *a.Tk_dev : a.Tk;
+    const int Tq = a.Tq;
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int q0 = blockIdx.x * kAttnQB;
+    const int nq = min(kAttnQB, Tq - q0);
+    if (nq <= 0) return;
+    int16_t *s = reinterpret_cast<int16_t *>(smem);                    // [QB][Tk]
+    uint8_t *pp = reinterpret_cast<uint8_t *>(s + kAttnQB * Tk);        // [QB][Tk]
+    __shared__ int32_t qv[kAttnQB][16];
+    __shared__ int32_t red[kAttnQB][kAttnThreads / 32];
+    __shared__ int32_t rowv[kAttnQB][2];
+    __shared__ int32_t pv_part[kAttnThreads / 32][kAttnQB][64];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < kAttnQB * 16) {
+        const int r = tid / 16, w = tid % 16;
+        int32_t val = 0;
+        if (r < nq) {
+            const int8_t *qr = a.q + (int64_t)b * a.q_bs + (int64_t)(q0 + r) * a.ldq + h * 64;
+            val = reinterpret_cast<const int32_t *>(qr)[w];
+        }
+        qv[r][w] = val;
+    }
+    __syncthreads();
+    // pass 1: scores + row max
+    int32_t lmax[kAttnQB];
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) lmax[r] = -32768;
+    const uint32_t qsh = (uint32_t)(a.qk_shift > 0 ? a.qk_shift : 0);
+    for (int j = tid; j < Tk; j += kAttnThreads) {
+        const int4 *kr = reinterpret_cast<const int4 *>(a.k + (int64_t)b * a.k_bs + (int64_t)j * a.ldk + h * 64);
+        int4 kk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) kk[u] = kr[u];
+        const int32_t *kw = reinterpret_cast<const int32_t *>(kk);
+#pragma unroll
+        for (int r = 0; r < kAttnQB; ++r) {
+            if (r < nq) {
+                const int qi = Tk - Tq + q0 + r;  // absolute query position
+                bool masked = false;
+                if (a.mask_mode == 1) masked = j > qi;
+                else if (a.mask_mode == 2) masked = a.mask[(int64_t)(q0 + r) * Tk + j] != 0;
+                int16_t sv = -32768;
+                if (!masked) {
+                    int32_t acc = 0;
+#pragma unroll
+                    for (int w = 0; w < 16; ++w) acc = __dp4a(kw[w], qv[r][w], acc);
+                    int32_t t = rrs(wmul(acc, (int32_t)a.qk_mult), qsh);
+                    sv = (int16_t)clampi(t, -32768, 32767);
+                    lmax[r] = max(lmax[r], (int32_t)sv);
+                }
+                s[r * Tk + j] = sv;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) {
+        int32_t m = warp_max(lmax[r]);
+        if (lane == 0) red[r][warp] = m;
+    }
+    __syncthreads();
+    if (tid < kAttnQB) {
+        int32_t m = -32768;
+        for (int w = 0; w < kAttnThreads / 32; ++w) m = max(m, red[tid][w]);
+        rowv[tid][0] = (int16_t)(m + 1);  // int16 wrap of row max + 1
+    }
+    __syncthreads();
+    // pass 2: shift-exp + row sum
+    int32_t lsum[kAttnQB];
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) lsum[r] = 0;
+    for (int j = tid; j < Tk; j += kAttnThreads) {
+#pragma unroll
+        for (int r = 0; r < kAttnQB; ++r) {
+            if (r < nq) {
+                const int qi = Tk - Tq + q0 + r;
+                bool masked = false;
+                if (a.mask_mode == 1) masked = j > qi;
+                else if (a.mask_mode == 2) masked = a.mask[(int64_t)(q0 + r) * Tk + j] != 0;
+                const int32_t e = masked ? 0 : shift_exp_one(s[r * Tk + j], rowv[r][0], a.frac_bits);
+                pp[r * Tk + j] = (uint8_t)e;
+                lsum[r] += e;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) {
+        int32_t v = warp_sum(lsum[r]);
+        if (lane == 0) red[r][warp] = v;
+    }
+    __syncthreads();
+    if (tid < kAttnQB) {
+        int32_t v = 0;
+        for (int w = 0; w < kAttnThreads / 32; ++w) v += red[tid][w];
+        rowv[tid][1] = v;
+    }
+    // pass 3: P.V. Warp w takes keys w, w+8, ...; lane owns dims 2l, 2l+1.
+    uint32_t acc[kAttnQB][2];
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) acc[r][0] = acc[r][1] = 0;
+    const int8_t *vb = a.v + (int64_t)b * a.v_bs + h * 64 + 2 * lane;
+    for (int j = warp; j < Tk; j += kAttnThreads / 32) {
+        const int16_t vv = *reinterpret_cast<const int16_t *>(vb + (int64_t)j * a.ldv);
+        const int32_t v0 = (int8_t)(vv & 0xFF), v1 = (int8_t)((vv >> 8) & 0xFF);
+#pragma unroll
+        for (int r = 0; r < kAttnQB; ++r) {
+            const int32_t p = pp[r * Tk + j];
+            acc[r][0] += (uint32_t)(p * v0);
+            acc[r][1] += (uint32_t)(p * v1);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kAttnQB; ++r) {
+        pv_part[warp][r][2 * lane] = (int32_t)acc[r][0];
+        pv_part[warp][r][2 * lane + 1] = (int32_t)acc[r][1];
+    }
+    __syncthreads();
+    const uint32_t avs = (uint32_t)clampi(a.av_shift, 0, 32);
+    for (int idx = tid; idx < kAttnQB * 64; idx += kAttnThreads) {
+        const int r = idx / 64, d = idx % 64;
+        if (r >= nq) continue;
+        uint32_t sum = 0;
+#pragma unroll
+        for (int w = 0; w < kAttnThreads / 32; ++w) sum += (uint32_t)pv_part[w][r][d];
+        const int32_t inv = fisr(rowv[r][1], a.rsqrt_offset);
+        int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
+        v = rrs(wmul(v, inv), a.rsqrt_offset);
+        v = rrs(wmul(v, (int32_t)a.av_mult), avs);
+        a.out[(int64_t)b * a.o_bs + (int64_t)(q0 + r) * a.ldo + h * 64 + d] = (int8_t)clampi(v, -127, 127);
+    }
+}
+
+cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
+    if (B <= 0 || H <= 0 || a.Tq <= 0) return cudaSuccess;
+    const int tk_cap = a.Tk_cap > 0 ? a.Tk_cap : a.Tk;
+    const size_t smem = (size_t)kAttnQB * tk_cap * 3;
+    static size_t smem_set = 0;
+    if (smem > 48 * 1024 && smem > smem_set) {
+        cudaError_t e = cudaFuncSetAttribute(attn_cc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        smem_set = smem;
+    }
+    dim3 grid((a.Tq + kAttnQB - 1) / kAttnQB, H, B);
+    attn_cc_kernel<<<grid, kAttnThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Reference-layout attention stages (attention_torch.cpp), any head_dim.
+// ---------------------------------------------------------------------------
+// qk_requant_rowmax_scalar (attention_scalar.cpp:216-343)
+__global__ void qk_rowmax_kernel(const int8_t *q, const int8_t *k, const uint8_t *mask, int16_t *qk, int16_t *rmax1,
+                                 int H, int Tq, int Tk, int D, uint32_t mult, uint32_t sh) {
+    const int64_t row = blockIdx.x;  // (b*H + h)*Tq + i
+    const int i = (int)(row % Tq);
+    const int64_t bh = row / Tq;
+    const int8_t *qr = q + row * D;
+    int32_t lm = -32768;
+    for (int j = threadIdx.x; j < Tk; j += blockDim.x) {
+        int16_t out;
+        if (mask && mask[(int64_t)i * Tk + j]) {
+            out = -32768;
+        } else {
+            const int8_t *kr = k + (bh * Tk + j) * D;
+            int32_t acc = 0;
+            for (int d = 0; d < D; ++d) acc += (int32_t)qr[d] * (int32_t)kr[d];
+            out = (int16_t)clampi(rrs(wmul(acc, (int32_t)mult), sh), -32768, 32767);
+            lm = max(lm, (int32_t)out);
+        }
+        qk[row * Tk + j] = out;
+    }
+    __shared__ int32_t red[32];
+    lm = warp_max(lm);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = lm;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t m = -32768;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
+        rmax1[row] = (int16_t)(m + 1);
+    }
+}
+
+cudaError_t qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, int16_t *qk, int16_t *rmax1,
+                              int B, int H, int Tq, int Tk, int D, uint8_t mult, int32_t shift, cudaStream_t st) {
+    const int64_t rows = (int64_t)B * H * Tq;
+    if (rows <= 0) return cudaSuccess;
+    qk_rowmax_kernel<<<(unsigned)rows, 128, 0, st>>>(q, k, mask, qk, rmax1, H, Tq, Tk, D, mult,
+                                                     (uint32_t)(shift > 0 ? shift : 0));
+    return cudaGetLastError();
+}
+
+// shift_exp_scalar (attention_scalar.cpp:388-560)
+__global__ void shift_exp_kernel(const int16_t *x, const int16_t *rmax1, const uint8_t *mask, uint8_t *p,
+                                 int32_t *rowsum, int Tq, int Tk, int fb) {
+    const int64_t row = blockIdx.x;
+    const int i = (int)(row % Tq);
+    const int32_t xm = rmax1[row];
+    int32_t ls = 0;
+    for (int j = threadIdx.x; j < Tk; j += blockDim.x) {
+        int32_t e = 0;
+        if (!(mask && mask[(int64_t)i * Tk + j])) e = shift_exp_one(x[row * Tk + j], xm, fb);
+        p[row * Tk + j] = (uint8_t)e;
+        ls += e;
+    }
+    __shared__ int32_t red[32];
+    ls = warp_sum(ls);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ls;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int32_t v = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[w];
+        rowsum[row] = v;
+    }
+}
+
+cudaError_t shift_exp(const int16_t *x, const int16_t *rmax1, const uint8_t *mask, uint8_t *p, int32_t *rowsum, int B,
+                      int H, int Tq, int Tk, int fb, cudaStream_t st) {
+    const int64_t rows = (int64_t)B * H * Tq;
+    if (rows <= 0) return cudaSuccess;
+    shift_exp_kernel<<<(unsigned)rows, 128, 0, st>>>(x, rmax1, mask, p, rowsum, Tq, Tk, fb);
+    return cudaGetLastError();
+}
+
+// pv_norm_requant_scalar (attention_scalar.cpp:676-813); negative row sums
+// are flagged in *bad (the reference throws).
+__global__ void pv_norm_kernel(const uint8_t *p, const int8_t *vt, const int32_t *rowsum, uint32_t avm, uint32_t avs,
+                               uint32_t off, int8_t *out, int H, int Tq, int Tk, int D, int *bad) {
+    const int64_t row = blockIdx.x;  // (b*H + h)*Tq + i
+    const int i = (int)(row % Tq);
+    const int64_t bh = row / Tq;
+    const int h = (int)(bh % H);
+    const int64_t b = bh / H;
+    const int32_t sum = rowsum[row];
+    if (sum < 0) {
+        if (threadIdx.x == 0) atomicExch(bad, 1);
+        return;
+    }
+    const int32_t inv = fisr(sum, off);
+    const uint8_t *pr = p + row * Tk;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const int8_t *vr = vt + (bh * D + d) * Tk;
+        uint32_t acc = 0;
+        for (int j = 0; j < Tk; ++j) acc += (uint32_t)((int32_t)pr[j] * (int32_t)vr[j]);
+        int32_t v = rrs(wmul((int32_t)acc, inv), off);
+        v = rrs(wmul(v, inv), off);
+        v = rrs(wmul(v, (int32_t)avm), avs);
+        out[((b * Tq + i) * H + h) * D + d] = (int8_t)clampi(v, -127, 127);
+    }
+}
+
+cudaError_t pv_norm_requant(const uint8_t *p, const int8_t *vt, const int32_t *rowsum, uint8_t av_mult,
+                            int8_t av_shift, uint32_t off, int8_t *out, int B, int H, int Tq, int Tk, int D, int *bad,
+                            cudaStream_t st) {
+    const int64_t rows = (int64_t)B * H * Tq;
+    if (rows <= 0) return cudaSuccess;
+    pv_norm_kernel<<<(unsigned)rows, 64, 0, st>>>(p, vt, rowsum, av_mult, (uint32_t)clampi(av_shift, 0, 32), off, out,
+                                                  H, Tq, Tk, D, bad);
+    return cudaGetLastError();
+}
+
+}  // namespace iw

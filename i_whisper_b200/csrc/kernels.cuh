@@ -1,0 +1,73 @@
+// kernels.cuh -- launchers of the bandwidth-bound kernels (kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace iw {
+
+struct LnParams {
+    int32_t ln_mult;       // u8 value
+    int32_t ln_shift;      // int8 value
+    uint32_t out_mult;     // u32
+    uint32_t out_shift;    // (uint32)(int32)int8: negative -> >= 32 -> 0
+    uint32_t rsqrt_offset; // 13 (LayerNorm_int.offset)
+};
+
+struct GeluParams {
+    const uint8_t *lut;
+    const uint8_t *mi;
+    const int8_t *si;
+    const uint8_t *mo;
+    const int8_t *so;
+    int n_in, n_out;
+};
+
+struct AttnArgs {
+    const int8_t *q;
+    int64_t ldq, q_bs;  // row stride, batch stride (elements)
+    const int8_t *k;
+    int64_t ldk, k_bs;
+    const int8_t *v;
+    int64_t ldv, v_bs;
+    int8_t *out;
+    int64_t ldo, o_bs;
+    int Tq, Tk;
+    const int32_t *Tk_dev;  // optional: key count read on the device
+    int Tk_cap;             // shared-memory capacity in keys (>= any Tk)
+    int mask_mode;          // 0 none, 1 causal (key j > Tk-Tq+i masked), 2 explicit [Tq,Tk]
+    const uint8_t *mask;
+    uint32_t qk_mult;
+    int32_t qk_shift;
+    int32_t frac_bits;
+    uint32_t av_mult;
+    int32_t av_shift;
+    uint32_t rsqrt_offset;
+};
+
+cudaError_t rowsum_i8(const int8_t *x, int64_t ldx, int M, int K, int32_t *out, cudaStream_t st);
+cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, const int32_t *beta, const LnParams &p,
+                        int8_t *y, int64_t ldy, int rows, int d, int32_t *rowsum_out, int32_t *rowsum_zero,
+                        cudaStream_t st);
+cudaError_t layernorm32_stats(const int16_t *x, int rows, int d, int32_t *mean, int32_t *var, int32_t *rs,
+                              cudaStream_t st);
+cudaError_t fisr_vec(const int32_t *x, int32_t *y, int64_t n, uint32_t off, cudaStream_t st);
+cudaError_t gelu(const int8_t *x, int8_t *y, int64_t n, int channels, const GeluParams &g, cudaStream_t st);
+cudaError_t residual15(const int32_t *br, const int16_t *r, uint16_t m, int16_t *y, int64_t n, cudaStream_t st);
+cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *addend, const uint16_t *mult,
+                          const int8_t *shift, int16_t *y, int B, int T, int C, int n_mult, int n_shift, int offset,
+                          const int32_t *offset_dev, cudaStream_t st);
+cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K, int stride, int pad, int Tout,
+                   int64_t ldo, int channels_last, cudaStream_t st);
+cudaError_t pad_rows(const int8_t *x, int64_t rows, int64_t cols, int8_t *out, int64_t ldo, cudaStream_t st);
+cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st);
+cudaError_t qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, int16_t *qk, int16_t *rmax1,
+                              int B, int H, int Tq, int Tk, int D, uint8_t mult, int32_t shift, cudaStream_t st);
+cudaError_t shift_exp(const int16_t *x, const int16_t *rmax1, const uint8_t *mask, uint8_t *p, int32_t *rowsum, int B,
+                      int H, int Tq, int Tk, int fb, cudaStream_t st);
+cudaError_t pv_norm_requant(const uint8_t *p, const int8_t *vt, const int32_t *rowsum, uint8_t av_mult,
+                            int8_t av_shift, uint32_t off, int8_t *out, int B, int H, int Tq, int Tk, int D, int *bad,
+                            cudaStream_t st);
+
+}  // namespace iw

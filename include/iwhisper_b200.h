@@ -1,0 +1,167 @@
+/*
+ * iwhisper_b200.h -- C ABI of the B200 (sm_100a) integer Whisper hot path.
+ *
+ * Drop-in boundary for the operator library the reference binds as
+ * `i_whisper.kernels._C` (vcsd-lab/I-Whisper,
+ * i_whisper/kernels/csrc/pybind.cpp:45-415). Each entry point computes
+ * exactly what the reference op of the same name computes (same integer
+ * semantics, bit for bit) with these differences in form:
+ *
+ *   - all array arguments are DEVICE pointers to contiguous row-major data
+ *     in the layouts of the reference op; outputs are caller-allocated;
+ *   - per-tensor scalar parameters (the 1-element tensors of the reference)
+ *     are passed by value;
+ *   - work is queued on `stream` (a cudaStream_t, NULL = legacy default
+ *     stream) and the call returns without synchronising, except where
+ *     noted;
+ *   - the return value is IW_OK (0) or a negative IW_E* code; the message
+ *     of the last failure on the calling thread is given by iw_last_error().
+ *     The reference raises RuntimeError/ValueError (TORCH_CHECK,
+ *     std::invalid_argument) in the same situations.
+ *
+ * Optional arrays (bias, weight_zero, mask) may be NULL, like the
+ * reference's std::optional<Tensor> arguments.
+ */
+#ifndef IWHISPER_B200_H
+#define IWHISPER_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IW_OK 0
+#define IW_EINVAL (-1)    /* bad shape / size / argument (TORCH_CHECK)      */
+#define IW_EVALUE (-2)    /* value error (std::invalid_argument)            */
+#define IW_ECUDA (-3)     /* CUDA runtime error                             */
+#define IW_EDEVICE (-4)   /* device-side wait gave up (see iw_device_status) */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *iw_last_error(void);
+/* ABI version of this library. */
+int iw_abi_version(void);
+/* Synchronises the device, returns the device status word in *status
+ * (bit 0: a bounded in-kernel wait timed out) and clears it if `clear`. */
+int iw_device_status(uint32_t *status, int clear);
+
+/* linear8_{scalar,simd} -- linear8_scalar.cpp:30-84; pybind.cpp:51-70.
+ * x [M,K] int8, weight [N,K] int8, bias [N] int32?, weight_zero [N] int8?,
+ * multiplier [N] uint32, shift [N] int8 -> y [M,N] int8. */
+int iw_linear8(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+               const uint32_t *multiplier, const int8_t *shift, int8_t *y, int64_t M, int64_t K, int64_t N,
+               void *stream);
+
+/* linear8_accum_{scalar,simd}_debug -- linear8_scalar.cpp:87-127;
+ * pybind.cpp:71-81. Same inputs, int32 accumulator out (no requant). */
+int iw_linear8_accum(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                     int32_t *y, int64_t M, int64_t K, int64_t N, void *stream);
+
+/* linear32_{scalar,simd} -- linear32_scalar.cpp:96-129 (requant of
+ * linear32_simd.cpp:231-255); pybind.cpp:82-101. -> y [M,N] int32. */
+int iw_linear32(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                const uint32_t *multiplier, const int8_t *shift, int32_t *y, int64_t M, int64_t K, int64_t N,
+                void *stream);
+
+/* Fused Linear32 + residual15: y = residual15(linear32(x), residual, m).
+ * Replaces the pair Linear32.forward (linear.py:118-187) ->
+ * residual15_* (model_int.py:1126-1171; residual15_scalar.cpp:9-27).
+ * residual/y [M,N] int16; y may alias residual (in-place update). */
+int iw_linear32_residual15(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                           const uint32_t *multiplier, const int8_t *shift, const int16_t *residual,
+                           uint16_t residual_multiplier, int16_t *y, int64_t M, int64_t K, int64_t N, void *stream);
+
+/* residual15_{scalar,simd} -- residual15_scalar.cpp:9-27; pybind.cpp:115-128. */
+int iw_residual15(const int32_t *branch, const int16_t *residual, uint16_t multiplier, int16_t *y, int64_t numel,
+                  void *stream);
+
+/* layernorm32_{scalar,simd} -- layernorm_scalar.cpp:464-624 with
+ * rsqrt offset 13 (layernorm_torch.cpp:265); pybind.cpp:130-151.
+ * x [rows,d] int16, d in {384,512,768,1024,1280} -> y [rows,d] int8. */
+int iw_layernorm32(const int16_t *x, const int8_t *weight, const int32_t *bias, uint8_t ln_multiplier,
+                   int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y, int64_t rows, int64_t d,
+                   void *stream);
+
+/* layernorm32_stats_{scalar,simd} -- layernorm_scalar.cpp:133-214;
+ * pybind.cpp:185-194. mean/variance/renorm_shift [rows] int32. */
+int iw_layernorm32_stats(const int16_t *x, int32_t *mean, int32_t *variance, int32_t *renorm_shift, int64_t rows,
+                         int64_t d, void *stream);
+
+/* layernorm32_rsqrt_scalar -- layernorm_scalar.cpp:383-437 (offset 13);
+ * pybind.cpp:195-200. Synchronises to check that every input is >= 0. */
+int iw_layernorm32_rsqrt(const int32_t *variance, int32_t *invstd, int64_t numel, void *stream);
+
+/* gelu_{scalar,simd} -- gelu_scalar.cpp:10-181; pybind.cpp:216-235.
+ * Parameters per channel (count == channels) or per tensor (count 1). */
+int iw_gelu(const int8_t *x, const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,
+            const uint8_t *luto_multiplier, const int8_t *luto_shift, int8_t *y, int64_t numel, int64_t channels,
+            int64_t luti_count, int64_t luto_count, void *stream);
+
+/* qk_requant_rowmax_{scalar,simd} -- attention_scalar.cpp:216-343;
+ * pybind.cpp:251-269. q [B,H,Tq,D], k [B,H,Tk,D] int8, mask [Tq,Tk]
+ * bool? -> qk [B,H,Tq,Tk] int16, row_max_plus1 [B,H,Tq] int16. */
+int iw_qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, uint8_t multiplier, int8_t shift,
+                         int16_t *qk, int16_t *row_max_plus1, int64_t B, int64_t H, int64_t Tq, int64_t Tk,
+                         int64_t D, void *stream);
+
+/* shift_exp_{scalar,simd} -- attention_scalar.cpp:388-560;
+ * pybind.cpp:271-287. frac_bits in [1,14). -> p uint8, row_sum int32. */
+int iw_shift_exp(const int16_t *x, const int16_t *row_max_plus1, const uint8_t *mask, int32_t frac_bits, uint8_t *p,
+                 int32_t *row_sum, int64_t B, int64_t H, int64_t Tq, int64_t Tk, void *stream);
+
+/* pv_norm_requant_{scalar,simd} -- attention_scalar.cpp:676-813;
+ * pybind.cpp:303-323. p [B,H,Tq,Tk] uint8, v [B,H,D,Tk] int8, row_sum
+ * [B,H,Tq] int32 -> y [B,Tq,H*D] int8. rsqrt_offset in [0,29].
+ * Synchronises; a negative row sum gives IW_EVALUE. */
+int iw_pv_norm_requant(const uint8_t *p, const int8_t *v, const int32_t *row_sum, uint8_t av_multiplier,
+                       int8_t av_shift, int64_t rsqrt_offset, int8_t *y, int64_t B, int64_t H, int64_t Tq,
+                       int64_t Tk, int64_t D, void *stream);
+
+/* Fused integer attention (A1-A3 of MultiHeadAttention_int.qkv_attention,
+ * model_int.py:774-1042) for head_dim 64, reading Q/K/V straight from the
+ * projection outputs: element (b,t,h,d) of Q is q[b*q_bs + t*ldq + h*64+d]
+ * (same for K, V with their strides); y[b*y_bs + t*ldy + h*64 + d].
+ * mask_mode 0: none, 1: causal (key j masked when j > Tk-Tq+i, the slice of
+ * TextDecoder_int.mask taken at model_int.py:786-799), 2: explicit mask
+ * [Tq,Tk]. Encoder-sized problems run on the tensor cores. */
+int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, int64_t ldk, int64_t k_bs,
+                 const int8_t *v, int64_t ldv, int64_t v_bs, int8_t *y, int64_t ldy, int64_t y_bs, int64_t B,
+                 int64_t H, int64_t Tq, int64_t Tk, int mask_mode, const uint8_t *mask, uint8_t qk_multiplier,
+                 int8_t qk_shift, int32_t frac_bits, uint8_t av_multiplier, int8_t av_shift, int64_t rsqrt_offset,
+                 void *stream);
+
+/* conv1d_{scalar,simd} -- conv1d_scalar.cpp:186-288; pybind.cpp:345-367.
+ * x [B,Cin,Tin] int8, weight [Cout,Cin*K] int8, bias [Cout] int32? ->
+ * y [B,Cout,Tout] int8, Tout = (Tin + 2*pad - K)/stride + 1. */
+int iw_conv1d(const int8_t *x, const int8_t *weight, const int32_t *bias, uint32_t multiplier, int8_t shift,
+              int64_t stride, int64_t padding, int8_t *y, int64_t B, int64_t Cin, int64_t Tin, int64_t Cout,
+              int64_t K, void *stream);
+
+/* add_requant15_{scalar,simd} -- add_requant15_scalar.cpp:29-80;
+ * pybind.cpp:369-384. x [B,T,C] int8, addend [T,C] int8, multiplier
+ * uint16 and shift int8 with 1 or C entries -> y [B,T,C] int16. */
+int iw_add_requant15(const int8_t *x, const int8_t *addend, const uint16_t *multiplier, const int8_t *shift,
+                     int16_t *y, int64_t B, int64_t T, int64_t C, int64_t multiplier_count, int64_t shift_count,
+                     void *stream);
+
+/* Token-embedding gather fused with add_requant15: the input row of
+ * (b,t) is table[tokens[b*T+t]] and the addend row is pe[offset + t]
+ * (TextDecoder_int.forward, model_int.py:1411-1428). */
+int iw_embed_add_requant15(const int8_t *table, const int64_t *tokens, const int8_t *pe, int64_t offset,
+                           const uint16_t *multiplier, const int8_t *shift, int16_t *y, int64_t B, int64_t T,
+                           int64_t C, int64_t multiplier_count, int64_t shift_count, void *stream);
+
+/* classifier_{scalar,simd} -- classifier_scalar.cpp:91-140;
+ * pybind.cpp:399-414. x [M,K] int8, weight [N,K] int8 -> y [M,N] int8. */
+int iw_classifier(const int8_t *x, const int8_t *weight, uint32_t multiplier, int8_t shift, int8_t *y, int64_t M,
+                  int64_t K, int64_t N, void *stream);
+
+/* Row sums of an int8 matrix [M,K] with row stride ldx (the sum(x) of the
+ * zero-point term, linear.py:89-91). */
+int iw_rowsum_i8(const int8_t *x, int64_t ldx, int64_t M, int64_t K, int32_t *y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IWHISPER_B200_H */

@@ -1,0 +1,289 @@
+"""Parity of every C-ABI operator with the oracle (bit-exact), on the GPU.
+
+Cases follow the reference's kernel tests (tests/kernels/test_*.py of
+vcsd-lab/I-Whisper): seeded random inputs, tails that are not multiples of
+the tile sizes, shift edge cases, multipliers up to 0xFFFFFFFF, masks, and
+the BASELINE microbench shapes at reduced M.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from i_whisper_b200 import ops as _ops
+    return _ops
+
+
+@pytest.fixture(scope="module")
+def L():
+    return O.lib("port")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+def rand_linear(rng, M, K, N, shift_lo=0, shift_hi=33):
+    x = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-128, 128, (N, K), dtype=np.int8)
+    b = rng.integers(-(2 ** 20), 2 ** 20, N, dtype=np.int32)
+    wz = rng.integers(-128, 128, N, dtype=np.int8)
+    m = rng.integers(0, 2 ** 32, N, dtype=np.uint32)
+    s = rng.integers(shift_lo, shift_hi, N).astype(np.int8)
+    return x, w, b, wz, m, s
+
+
+LIN_SHAPES = [(1, 16, 16), (7, 100, 29), (128, 128, 256), (130, 384, 384), (300, 1024, 1024),
+              (257, 1024, 4096), (129, 4096, 1024), (64, 1280, 5120), (1500, 384, 1152)]
+
+
+@pytest.mark.parametrize("M,K,N", LIN_SHAPES)
+@pytest.mark.parametrize("with_bias,with_zero", [(True, True), (False, False), (True, False)])
+def test_linear8(ops, L, M, K, N, with_bias, with_zero):
+    rng = np.random.default_rng(M * 7 + K + N)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=-3)
+    b = b if with_bias else None
+    wz = wz if with_zero else None
+    ref = L.linear8(x, w, b, wz, m, s)
+    got = ops.linear8_cuda(dev(x), dev(w), None if b is None else dev(b), None if wz is None else dev(wz), dev(m), dev(s))
+    assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("M,K,N", LIN_SHAPES[:6])
+def test_linear8_accum(ops, L, M, K, N):
+    rng = np.random.default_rng(5 + M)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N)
+    ref = L.linear8_accum(x, w, b, wz)
+    got = ops.linear8_accum_cuda_debug(dev(x), dev(w), dev(b), dev(wz))
+    assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("M,K,N", LIN_SHAPES)
+def test_linear32(ops, L, M, K, N):
+    rng = np.random.default_rng(11 + M + N)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=0, shift_hi=40)
+    ref = L.linear32(x, w, b, wz, m, s)
+    got = ops.linear32_cuda(dev(x), dev(w), dev(b), dev(wz), dev(m), dev(s))
+    assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(7, 100, 29), (300, 1024, 1024), (129, 4096, 1024), (1500, 384, 384)])
+def test_linear32_residual15(ops, L, M, K, N):
+    rng = np.random.default_rng(3 + M)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=0, shift_hi=12)
+    r = rng.integers(-16383, 16384, (M, N), dtype=np.int16)
+    rm = 40000
+    ref = L.residual15(L.linear32(x, w, b, wz, m, s), r, rm)
+    got = ops.linear32_residual15_cuda(dev(x), dev(w), dev(b), dev(wz), dev(m), dev(s), dev(r), rm)
+    assert np.array_equal(host(got), ref)
+
+
+def test_residual15(ops, L):
+    rng = np.random.default_rng(9)
+    br = rng.integers(-(2 ** 31), 2 ** 31, 100003, dtype=np.int32)
+    r = rng.integers(-32768, 32768, 100003, dtype=np.int16)
+    for mult in (0, 1, 32768, 65535):
+        ref = L.residual15(br, r, mult)
+        got = ops.residual15_cuda(dev(br), dev(r), torch.tensor([mult], dtype=torch.uint16))
+        assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("d", [384, 512, 768, 1024, 1280])
+@pytest.mark.parametrize("rows", [1, 33, 1500])
+def test_layernorm32(ops, L, d, rows):
+    rng = np.random.default_rng(d + rows)
+    x = rng.integers(-16383, 16384, (rows, d), dtype=np.int16)
+    x[0] = x[0] // 64  # small dynamic range row
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    for (lm, ls, om, os) in [(200, 5, 2 ** 31 + 12345, 7), (255, 0, 0xFFFFFFFF, 0), (1, 20, 123456789, 31), (37, -2, 2 ** 30, -1)]:
+        ref = L.layernorm32(x, g, be, lm, ls, om, os)
+        got = ops.layernorm32_cuda(dev(x), dev(g), dev(be), torch.tensor([lm], dtype=torch.uint8),
+                                   torch.tensor([ls], dtype=torch.int8), torch.tensor([om], dtype=torch.uint32),
+                                   torch.tensor([os], dtype=torch.int8))
+        assert np.array_equal(host(got), ref), (lm, ls, om, os)
+    ref = L.layernorm32(x, g, None, 200, 5, 2 ** 31, 7)
+    got = ops.layernorm32_cuda(dev(x), dev(g), None, 200, 5, 2 ** 31, 7)
+    assert np.array_equal(host(got), ref)
+    for a, b in zip(L.layernorm32_stats(x), ops.layernorm32_stats_cuda(dev(x))):
+        assert np.array_equal(host(b), a)
+
+
+def test_layernorm32_zero_rows(ops, L):
+    x = np.zeros((4, 512), np.int16)
+    g = np.ones(512, np.int8)
+    ref = L.layernorm32(x, g, None, 128, 6, 2 ** 31, 8)
+    got = ops.layernorm32_cuda(dev(x), dev(g), None, 128, 6, 2 ** 31, 8)
+    assert np.array_equal(host(got), ref)
+
+
+def test_rsqrt(ops, L):
+    vals = {0}
+    for bit in range(0, 31):
+        for dlt in (-1, 0, 1):
+            v = (1 << bit) + dlt
+            if 0 <= v <= 2 ** 31 - 1:
+                vals.add(v)
+    rng = np.random.default_rng(1)
+    v = np.array(sorted(vals) + list(rng.integers(0, 1_000_000_001, 257)), np.int32)
+    assert np.array_equal(host(ops.layernorm32_rsqrt_cuda(dev(v))), L.fisr(v, 13))
+    with pytest.raises(ValueError):
+        ops.layernorm32_rsqrt_cuda(dev(np.array([1, -1], np.int32)))
+
+
+@pytest.mark.parametrize("C,ni,no", [(64, 64, 64), (4096, 4096, 4096), (3000, 1, 1), (1024, 1, 1024), (7, 1, 7)])
+def test_gelu(ops, L, C, ni, no):
+    rng = np.random.default_rng(C + ni + no)
+    x = rng.integers(-128, 128, (9, C), dtype=np.int8)
+    lut = rng.integers(0, 256, 16, dtype=np.uint8)
+    mi = rng.integers(0, 256, ni, dtype=np.uint8); si = rng.integers(-3, 35, ni).astype(np.int8)
+    mo = rng.integers(0, 256, no, dtype=np.uint8); so = rng.integers(-3, 35, no).astype(np.int8)
+    ref = L.gelu(x, lut, mi, si, mo, so)
+    got = ops.gelu_cuda(dev(x), dev(lut), dev(mi), dev(si), dev(mo), dev(so))
+    assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("D", [1, 7, 16, 17, 64])
+@pytest.mark.parametrize("Tq,Tk", [(1, 1), (3, 3), (5, 65), (1, 448), (17, 130)])
+@pytest.mark.parametrize("masked", [False, True])
+def test_attention_stages(ops, L, D, Tq, Tk, masked):
+    rng = np.random.default_rng(D * 100 + Tq * 10 + Tk)
+    B, H = 2, 3
+    q = rng.integers(-127, 128, (B, H, Tq, D), dtype=np.int8)
+    k = rng.integers(-127, 128, (B, H, Tk, D), dtype=np.int8)
+    vt = rng.integers(-127, 128, (B, H, D, Tk), dtype=np.int8)
+    mask = (rng.random((Tq, Tk)) < 0.3) if masked else None
+    mask_np = None if mask is None else mask.astype(np.uint8)
+    mask_t = None if mask is None else torch.from_numpy(mask).cuda()
+    for shift in (-3, 0, 1, 7, 31, 32):
+        qk_r, rm_r = L.qk_requant_rowmax(q, k, mask_np, 77, shift)
+        qk_g, rm_g = ops.qk_requant_rowmax_cuda(dev(q), dev(k), mask_t, torch.tensor([77], dtype=torch.uint8),
+                                                torch.tensor([shift], dtype=torch.int8))
+        assert np.array_equal(host(qk_g), qk_r) and np.array_equal(host(rm_g), rm_r), shift
+    qk_r, rm_r = L.qk_requant_rowmax(q, k, mask_np, 77, 9)
+    for fb in (1, 7, 9, 13):
+        p_r, s_r = L.shift_exp(qk_r, rm_r, mask_np, fb)
+        p_g, s_g = ops.shift_exp_cuda(dev(qk_r), dev(rm_r), mask_t, torch.tensor([fb], dtype=torch.int32))
+        assert np.array_equal(host(p_g), p_r) and np.array_equal(host(s_g), s_r), fb
+    p_r, s_r = L.shift_exp(qk_r, rm_r, mask_np, 7)
+    for av_s in (-2, 0, 9, 33):
+        y_r = L.pv_norm_requant(p_r, vt, s_r, 150, av_s, 16)
+        y_g = ops.pv_norm_requant_cuda(dev(p_r), dev(vt), dev(s_r), torch.tensor([150], dtype=torch.uint8),
+                                       torch.tensor([av_s], dtype=torch.int8), 16)
+        assert np.array_equal(host(y_g), y_r), av_s
+
+
+def test_pv_norm_negative_rowsum_raises(ops):
+    p = torch.zeros(1, 1, 2, 4, dtype=torch.uint8, device="cuda")
+    v = torch.zeros(1, 1, 8, 4, dtype=torch.int8, device="cuda")
+    rs = torch.tensor([0, -1], dtype=torch.int32, device="cuda").reshape(1, 1, 2, 1)
+    with pytest.raises(ValueError):
+        ops.pv_norm_requant_cuda(p, v, rs, torch.tensor([1], dtype=torch.uint8), torch.tensor([0], dtype=torch.int8), 16)
+
+
+@pytest.mark.parametrize("B,H,Tq,Tk,mode", [(2, 6, 1, 1500, 0), (3, 16, 1, 37, 1), (2, 8, 3, 3, 1), (1, 6, 40, 300, 0),
+                                            (2, 4, 5, 9, 2), (1, 16, 130, 130, 0)])
+def test_fused_attention(ops, L, B, H, Tq, Tk, mode):
+    rng = np.random.default_rng(B + H + Tq + Tk + mode)
+    d = H * 64
+    q = rng.integers(-127, 128, (B, Tq, d), dtype=np.int8)
+    k = rng.integers(-127, 128, (B, Tk, d), dtype=np.int8)
+    v = rng.integers(-127, 128, (B, Tk, d), dtype=np.int8)
+    P = {"a.qk_req_multiplier": np.array([90], np.uint8), "a.qk_req_shiftmount": np.array([10], np.int8),
+         "a.qk_frac_bits": np.array(7, np.int32), "a.av_req_multiplier": np.array([200], np.uint8),
+         "a.av_req_shiftmount": np.array([8], np.int8)}
+    mask = None
+    if mode == 1:
+        mask = np.triu(np.ones((Tk, Tk), np.uint8), 1)
+    elif mode == 2:
+        mask = (rng.random((Tq, Tk)) < 0.3).astype(np.uint8)
+    ref = O.attention_core(L, P, "a", q, k, v, H, mask if mode != 2 else None) if mode != 2 else None
+    if mode == 2:
+        q4 = q.reshape(B, Tq, H, 64).transpose(0, 2, 1, 3); k4 = k.reshape(B, Tk, H, 64).transpose(0, 2, 1, 3)
+        vt = v.reshape(B, Tk, H, 64).transpose(0, 2, 3, 1)
+        s, rm = L.qk_requant_rowmax(q4, k4, mask, 90, 10)
+        p, rs = L.shift_exp(s, rm, mask, 7)
+        ref = L.pv_norm_requant(p, vt, rs, 200, 8, 16)
+    got = ops.attention_cuda(dev(q), dev(k), dev(v), H, 90, 10, 7, 200, 8, 16, mask_mode=mode,
+                             mask=None if mode != 2 else dev(mask))
+    assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("B,Cin,Tin,Cout,stride", [(1, 80, 3000, 384, 1), (2, 384, 3000, 384, 2), (1, 7, 33, 5, 1),
+                                                   (2, 16, 50, 40, 2), (1, 128, 200, 64, 1)])
+def test_conv1d(ops, L, B, Cin, Tin, Cout, stride):
+    rng = np.random.default_rng(Cin + Tin)
+    x = rng.integers(-127, 128, (B, Cin, Tin), dtype=np.int8)
+    w = rng.integers(-127, 128, (Cout, Cin * 3), dtype=np.int8)
+    b = rng.integers(-5000, 5000, Cout, dtype=np.int32)
+    for m, s in [(2 ** 30 + 5, 6), (0xFFFFFFFF, 0), (123456, -2)]:
+        ref = L.conv1d(x, w, b, m, s, stride, 1)
+        got = ops.conv1d_cuda(dev(x), dev(w), dev(b), torch.tensor([m], dtype=torch.uint32),
+                              torch.tensor([s], dtype=torch.int8), stride, 1)
+        assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("nm,ns", [(1, 1), (64, 64), (1, 64)])
+def test_add_requant15(ops, L, nm, ns):
+    rng = np.random.default_rng(nm + ns)
+    x = rng.integers(-128, 128, (3, 30, 64), dtype=np.int8)
+    pe = rng.integers(-128, 128, (30, 64), dtype=np.int8)
+    mu = rng.integers(0, 65536, nm, dtype=np.uint16)
+    su = rng.integers(-3, 34, ns).astype(np.int8)
+    ref = L.add_requant15(x, pe, mu, su)
+    got = ops.add_requant15_cuda(dev(x), dev(pe), dev(mu), dev(su))
+    assert np.array_equal(host(got), ref)
+
+
+def test_embed_add_requant15(ops, L):
+    rng = np.random.default_rng(4)
+    table = rng.integers(-128, 128, (1000, 384), dtype=np.int8)
+    pe = rng.integers(-128, 128, (448, 384), dtype=np.int8)
+    tok = rng.integers(0, 1000, (5, 3)).astype(np.int64)
+    mu = np.array([200], np.uint16); su = np.array([3], np.int8)
+    for off in (0, 7, 445):
+        ref = L.add_requant15(table[tok], pe[off:off + 3], mu, su)
+        got = ops.embed_add_requant15_cuda(dev(table), dev(tok), dev(pe), off, dev(mu), dev(su))
+        assert np.array_equal(host(got), ref)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 384, 51865), (4, 1024, 51865), (3, 100, 77), (256, 1280, 51866)])
+def test_classifier(ops, L, M, K, N):
+    rng = np.random.default_rng(M + K)
+    x = rng.integers(-127, 128, (1, M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    for m, s in [(3 * 2 ** 30, 3), (2 ** 31, 9), (12345, -1)]:
+        ref = L.classifier(x, w, m, s)
+        got = ops.classifier_cuda(dev(x), dev(w), torch.tensor([m], dtype=torch.uint32), torch.tensor([s], dtype=torch.int8))
+        assert np.array_equal(host(got), ref)
+
+
+def test_error_paths(ops):
+    x = torch.zeros(2, 16, dtype=torch.int8, device="cuda")
+    w = torch.zeros(4, 16, dtype=torch.int8, device="cuda")
+    m = torch.ones(4, dtype=torch.uint32, device="cuda"); s = torch.zeros(4, dtype=torch.int8, device="cuda")
+    with pytest.raises(RuntimeError):
+        ops.linear8_cuda(x.int(), w, None, None, m, s)
+    with pytest.raises(RuntimeError):
+        ops.linear8_cuda(x, torch.zeros(4, 15, dtype=torch.int8, device="cuda"), None, None, m, s)
+    with pytest.raises(RuntimeError):
+        ops.linear8_cuda(x.cpu(), w, None, None, m, s)
+    with pytest.raises(RuntimeError):
+        ops.layernorm32_cuda(torch.zeros(2, 100, dtype=torch.int16, device="cuda"),
+                             torch.zeros(100, dtype=torch.int8, device="cuda"), None, 1, 0, 1, 0)
+
+
+def test_device_status_clean():
+    from i_whisper_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
