@@ -45,7 +45,57 @@ SIGNATURES = {
     "iw_rowsum_i8": [_P, _I64, _I64, _I64, _P, _P],
     "iw_device_status": [C.POINTER(C.c_uint32), C.c_int],
     "iw_abi_version": [],
+    "iw_gemm_i8": [_P, _P],
+    "iw_attention_ex": [_P, _P],
+    "iw_layernorm32_ex": [_P, _I64, _P, _P, _U8, _I8, _U32, _I8, _P, _I64, _I64, _I64, _P, _P, _P],
+    "iw_im2col": [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P],
+    "iw_embed_add_requant15_dev": [_P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
+    "iw_kv_append": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
+    "iw_greedy_step": [_P, _I64, _P],
+    "iw_add_i32": [_P, _I32, _P],
 }
+
+IW_GEMM_ACC32, IW_GEMM_INT8, IW_GEMM_LINEAR32, IW_GEMM_LINEAR32_RES = 0, 1, 2, 3
+
+
+class GemmDesc(C.Structure):
+    """``iw_gemm_desc`` (include/iwhisper_b200.h)."""
+    _fields_ = [
+        ("x", _P), ("ldx", _I64), ("w", _P), ("ldw", _I64), ("M", _I64), ("N", _I64), ("K", _I64),
+        ("mode", C.c_int), ("out", _P), ("ldo", _I64),
+        ("bias", _P), ("weight_zero", _P), ("x_rowsum", _P), ("multiplier", _P), ("shift", _P),
+        ("scalar_multiplier", _U32), ("scalar_shift", _I32),
+        ("lut", _P), ("luti_multiplier", _P), ("luti_shift", _P), ("luto_multiplier", _P), ("luto_shift", _P),
+        ("luti_per_channel", C.c_int), ("luto_per_channel", C.c_int),
+        ("residual", _P), ("ldr", _I64), ("residual_multiplier", _U32),
+        ("pos", _P), ("pos_T", _I64), ("pos_multiplier", _P), ("pos_shift", _P), ("pos_per_channel", C.c_int),
+        ("transpose_T", _I64), ("headmajor_T", _I64), ("headmajor_B", _I64),
+        ("out_rowsum", _P), ("tile_n", C.c_int),
+    ]
+
+
+class AttnDesc(C.Structure):
+    """``iw_attn_desc`` (include/iwhisper_b200.h)."""
+    _fields_ = [
+        ("q", _P), ("ldq", _I64), ("q_bs", _I64), ("q_hs", _I64),
+        ("k", _P), ("ldk", _I64), ("k_bs", _I64), ("k_hs", _I64),
+        ("v", _P), ("ldv", _I64), ("v_bs", _I64), ("v_hs", _I64),
+        ("y", _P), ("ldy", _I64), ("y_bs", _I64), ("y_hs", _I64),
+        ("B", _I64), ("H", _I64), ("Tq", _I64), ("Tk", _I64),
+        ("Tk_dev", _P), ("Tk_cap", _I64), ("mask_mode", C.c_int), ("mask", _P),
+        ("qk_multiplier", _U8), ("qk_shift", _I8), ("frac_bits", _I32),
+        ("av_multiplier", _U8), ("av_shift", _I8), ("rsqrt_offset", _I32),
+    ]
+
+
+class GreedyDesc(C.Structure):
+    """``iw_greedy_desc`` (include/iwhisper_b200.h)."""
+    _fields_ = [
+        ("logits", _P), ("ld", _I64), ("V", _I64), ("alpha", C.c_float),
+        ("suppress_bits", _P), ("blank", _P), ("n_blank", _I64),
+        ("eot", _I64), ("timestamp_begin", _I64), ("no_timestamps", _I64), ("max_initial_timestamp_index", _I64),
+        ("state", _P), ("tokens", _P), ("ld_tok", _I64), ("step_dev", _P), ("next", _P),
+    ]
 
 
 class IWhisperError(RuntimeError):

@@ -354,4 +354,141 @@ int iw_rowsum_i8(const int8_t *x, int64_t ldx, int64_t M, int64_t K, int32_t *y,
     return cuda_check(iw::rowsum_i8(x, ldx, (int)M, (int)K, y, S(stream)), "iw_rowsum_i8");
 }
 
+int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
+    if (!d) return fail(IW_EINVAL, "iw_gemm_i8: null descriptor");
+    if (d->M < 0 || d->N <= 0 || d->K <= 0 || d->M > INT32_MAX || d->N > INT32_MAX || d->K > INT32_MAX)
+        return fail(IW_EINVAL, "iw_gemm_i8: invalid shape M=%lld N=%lld K=%lld", (long long)d->M, (long long)d->N,
+                    (long long)d->K);
+    if (d->M == 0) return IW_OK;
+    if (d->K % 16 || d->ldx % 16 || d->ldw % 16)
+        return fail(IW_EINVAL, "iw_gemm_i8: K and the row strides must be multiples of 16");
+    if (d->weight_zero && !d->x_rowsum) return fail(IW_EINVAL, "iw_gemm_i8: weight_zero needs x_rowsum");
+    if (d->mode < 0 || d->mode > 3) return fail(IW_EINVAL, "iw_gemm_i8: bad mode %d", d->mode);
+    if ((d->mode == IW_GEMM_LINEAR32 || d->mode == IW_GEMM_LINEAR32_RES) && (!d->multiplier || !d->shift))
+        return fail(IW_EINVAL, "iw_gemm_i8: Linear32 needs per-channel multiplier and shift");
+    if (d->mode == IW_GEMM_LINEAR32_RES && !d->residual) return fail(IW_EINVAL, "iw_gemm_i8: residual is required");
+    if ((d->headmajor_T || d->transpose_T) && d->mode != IW_GEMM_INT8)
+        return fail(IW_EINVAL, "iw_gemm_i8: layouts apply to int8 outputs");
+    if (d->headmajor_T && (d->N % 64 || d->headmajor_B <= 0 || d->M != d->headmajor_B * d->headmajor_T))
+        return fail(IW_EINVAL, "iw_gemm_i8: head-major layout needs N%%64==0 and M == B*T");
+    if (d->transpose_T && d->M % d->transpose_T) return fail(IW_EINVAL, "iw_gemm_i8: M must be a multiple of T");
+    iw::EpiParams p;
+    p.out = d->out;
+    p.ldo = d->ldo;
+    p.bias = d->bias;
+    p.wz = d->weight_zero;
+    p.rowsum = d->x_rowsum;
+    if (d->multiplier) {
+        p.per_channel = 1;
+        p.mult = d->multiplier;
+        p.shift = d->shift;
+    } else {
+        p.per_channel = 0;
+        p.smult = d->scalar_multiplier;
+        p.sshift = (uint32_t)(d->scalar_shift > 0 ? d->scalar_shift : 0);
+    }
+    if (d->lut) {
+        p.gelu = 1;
+        p.lut = d->lut;
+        p.gmi = d->luti_multiplier;
+        p.gsi = d->luti_shift;
+        p.gmo = d->luto_multiplier;
+        p.gso = d->luto_shift;
+        p.gelu_in_pc = d->luti_per_channel;
+        p.gelu_out_pc = d->luto_per_channel;
+    }
+    p.res = d->residual;
+    p.ldr = d->ldr;
+    p.res_mult = d->residual_multiplier;
+    if (d->pos) {
+        p.posadd = 1;
+        p.pe = d->pos;
+        p.pe_T = (int)d->pos_T;
+        p.pm = d->pos_multiplier;
+        p.ps = d->pos_shift;
+        p.pos_pc = d->pos_per_channel;
+    }
+    p.transpose_T = (int)d->transpose_T;
+    p.hm_T = (int)d->headmajor_T;
+    p.hm_B = (int)d->headmajor_B;
+    p.rowsum_out = d->out_rowsum;
+    iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
+    return cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8");
+}
+
+int iw_attention_ex(const iw_attn_desc *d, void *stream) {
+    if (!d) return fail(IW_EINVAL, "iw_attention_ex: null descriptor");
+    if (d->B < 0 || d->H < 0 || d->Tq < 0 || d->Tk < 0) return fail(IW_EINVAL, "iw_attention_ex: invalid shape");
+    if (!(d->frac_bits > 0 && d->frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    if (!(d->rsqrt_offset >= 0 && d->rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
+    if (d->mask_mode == 2 && !d->mask) return fail(IW_EINVAL, "iw_attention_ex: mask_mode 2 needs a mask");
+    if (((d->ldq | d->ldk | d->q_bs | d->k_bs | d->q_hs | d->k_hs) & 15) ||
+        ((reinterpret_cast<uintptr_t>(d->q) | reinterpret_cast<uintptr_t>(d->k)) & 15) ||
+        ((d->ldv | d->v_bs | d->v_hs | reinterpret_cast<uintptr_t>(d->v)) & 1))
+        return fail(IW_EINVAL, "iw_attention_ex: Q/K rows must be 16-byte aligned");
+    iw::AttnArgs a;
+    a.q = d->q; a.ldq = d->ldq; a.q_bs = d->q_bs; a.q_hs = d->q_hs;
+    a.k = d->k; a.ldk = d->ldk; a.k_bs = d->k_bs; a.k_hs = d->k_hs;
+    a.v = d->v; a.ldv = d->ldv; a.v_bs = d->v_bs; a.v_hs = d->v_hs;
+    a.out = d->y; a.ldo = d->ldy; a.o_bs = d->y_bs; a.o_hs = d->y_hs;
+    a.Tq = (int)d->Tq; a.Tk = (int)d->Tk; a.Tk_dev = d->Tk_dev;
+    a.Tk_cap = (int)(d->Tk_cap > 0 ? d->Tk_cap : d->Tk);
+    a.mask_mode = d->mask_mode; a.mask = d->mask;
+    a.qk_mult = d->qk_multiplier; a.qk_shift = d->qk_shift; a.frac_bits = d->frac_bits;
+    a.av_mult = d->av_multiplier; a.av_shift = d->av_shift; a.rsqrt_offset = (uint32_t)d->rsqrt_offset;
+    return cuda_check(iw::attention_cc(a, (int)d->B, (int)d->H, S(stream)), "iw_attention_ex");
+}
+
+int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
+                      uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
+                      int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    iw::LnParams p{(int32_t)ln_multiplier, (int32_t)ln_shift, out_multiplier, (uint32_t)(int32_t)out_shift, 13u};
+    return cuda_check(
+        iw::layernorm32(x, ldx, weight, bias, p, y, ldy, (int)rows, (int)d, rowsum_out, rowsum_zero, S(stream)),
+        "iw_layernorm32_ex");
+}
+
+int iw_im2col(const int8_t *x, int8_t *out, int64_t B, int64_t Cin, int64_t Tin, int64_t K, int64_t stride,
+              int64_t pad, int64_t Tout, int64_t ldo, int channels_last, void *stream) {
+    if (ldo < Cin * K) return fail(IW_EINVAL, "iw_im2col: ldo < Cin*K");
+    return cuda_check(iw::im2col(x, out, (int)B, (int)Cin, (int)Tin, (int)K, (int)stride, (int)pad, (int)Tout, ldo,
+                                 channels_last, S(stream)),
+                      "iw_im2col");
+}
+
+int iw_embed_add_requant15_dev(const int8_t *table, const int64_t *tokens, const int8_t *pe,
+                               const int32_t *offset_dev, int64_t offset, const uint16_t *multiplier,
+                               const int8_t *shift, int16_t *y, int64_t B, int64_t T, int64_t C,
+                               int64_t multiplier_count, int64_t shift_count, void *stream) {
+    if (!(multiplier_count == 1 || multiplier_count == C)) return fail(IW_EINVAL, "multiplier must contain 1 or C elements");
+    if (!(shift_count == 1 || shift_count == C)) return fail(IW_EINVAL, "shift must contain 1 or C elements");
+    return cuda_check(iw::add_requant15(table, tokens, pe, multiplier, shift, y, (int)B, (int)T, (int)C,
+                                        (int)multiplier_count, (int)shift_count, (int)offset, offset_dev, S(stream)),
+                      "iw_embed_add_requant15_dev");
+}
+
+int iw_kv_append(const int8_t *src, int64_t lds, int64_t k_col, int64_t v_col, int8_t *k_cache, int8_t *v_cache,
+                 int64_t B, int64_t H, int64_t T, int64_t Tcap, int64_t pos, const int32_t *pos_dev, void *stream) {
+    if ((lds | k_col | v_col) & 3) return fail(IW_EINVAL, "iw_kv_append: columns must be 4-byte aligned");
+    return cuda_check(iw::kv_append(src, lds, (int)k_col, (int)v_col, k_cache, v_cache, (int)B, (int)H, (int)T,
+                                    (int)Tcap, (int)pos, pos_dev, S(stream)),
+                      "iw_kv_append");
+}
+
+int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream) {
+    if (!d) return fail(IW_EINVAL, "iw_greedy_step: null descriptor");
+    iw::GreedyArgs g;
+    g.logits = d->logits; g.ld = d->ld; g.V = (int)d->V; g.alpha = d->alpha;
+    g.suppress_bits = d->suppress_bits; g.blank = d->blank; g.n_blank = (int)d->n_blank;
+    g.eot = (int)d->eot; g.timestamp_begin = (int)d->timestamp_begin; g.no_timestamps = (int)d->no_timestamps;
+    g.max_initial_timestamp_index = (int)d->max_initial_timestamp_index;
+    g.state = d->state; g.tokens = d->tokens; g.ld_tok = d->ld_tok; g.step_dev = d->step_dev; g.next = d->next;
+    return cuda_check(iw::greedy_step(g, (int)B, S(stream)), "iw_greedy_step");
+}
+
+int iw_add_i32(int32_t *p, int32_t v, void *stream) {
+    return cuda_check(iw::add_i32(p, v, S(stream)), "iw_add_i32");
+}
+
 }  // extern "C"

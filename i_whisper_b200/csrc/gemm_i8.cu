@@ -180,6 +180,24 @@ IW_DEV void epi_chunk(const EpiParams &p, int m, int n0, const uint32_t (&acc)[3
                 if (n0 + j < N) base[((int64_t)b * N + n0 + j) * p.transpose_T + t] = (int8_t)v[j];
             return;
         }
+        if (p.hm_T) {
+            const int b = m / p.hm_T, t = m % p.hm_T;
+            const int g = n0 >> 6;
+            int8_t *out = base + (((int64_t)g * p.hm_B + b) * p.hm_T + t) * 64 + (n0 & 63);
+            if (full) {
+                uint32_t w[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    w[q] = (uint32_t)(uint8_t)v[4 * q] | ((uint32_t)(uint8_t)v[4 * q + 1] << 8) |
+                           ((uint32_t)(uint8_t)v[4 * q + 2] << 16) | ((uint32_t)(uint8_t)v[4 * q + 3] << 24);
+                *reinterpret_cast<uint4 *>(out) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4 *>(out + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                for (int j = 0; j < 32; ++j)
+                    if (n0 + j < N) out[j] = (int8_t)v[j];
+            }
+            return;
+        }
         if (p.vt_T) {
             const int b = m / p.vt_T, t = m % p.vt_T;
             const int H = N / p.vt_D;

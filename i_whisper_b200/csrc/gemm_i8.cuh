@@ -54,6 +54,10 @@ struct EpiParams {
     // optional: per-head transposed store for attention V^T:
     // out[(b*H + h)*D + d][t] with m = b*T + t, n = h*D + d, row stride ldo
     int vt_T = 0, vt_D = 0;
+    // optional: head-major store for K/V caches: column n belongs to head
+    // group g = n / 64; row m = b*hm_T + t goes to
+    // out[((g*hm_B + b)*hm_T + t)*64 + n%64]
+    int hm_T = 0, hm_B = 0;
     // optional: accumulate per-row sums of the int8 output (next GEMM's
     // zero-point term)
     int32_t *rowsum_out = nullptr;

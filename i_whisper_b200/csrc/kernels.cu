@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
         const int r = tid / 16, w = tid % 16;
         int32_t val = 0;
         if (r < nq) {
-            const int8_t *qr = a.q + (int64_t)b * a.q_bs + (int64_t)(q0 + r) * a.ldq + h * 64;
+            const int8_t *qr = a.q + (int64_t)b * a.q_bs + (int64_t)(q0 + r) * a.ldq + (int64_t)h * a.q_hs;
             val = reinterpret_cast<const int32_t *>(qr)[w];
         }
         qv[r][w] = val;
@@ -417,7 +417,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     for (int r = 0; r < kAttnQB; ++r) lmax[r] = -32768;
     const uint32_t qsh = (uint32_t)(a.qk_shift > 0 ? a.qk_shift : 0);
     for (int j = tid; j < Tk; j += kAttnThreads) {
-        const int4 *kr = reinterpret_cast<const int4 *>(a.k + (int64_t)b * a.k_bs + (int64_t)j * a.ldk + h * 64);
+        const int4 *kr = reinterpret_cast<const int4 *>(a.k + (int64_t)b * a.k_bs + (int64_t)j * a.ldk + (int64_t)h * a.k_hs);
         int4 kk[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) kk[u] = kr[u];
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     uint32_t acc[kAttnQB][2];
 #pragma unroll
     for (int r = 0; r < kAttnQB; ++r) acc[r][0] = acc[r][1] = 0;
-    const int8_t *vb = a.v + (int64_t)b * a.v_bs + h * 64 + 2 * lane;
+    const int8_t *vb = a.v + (int64_t)b * a.v_bs + (int64_t)h * a.v_hs + 2 * lane;
     for (int j = warp; j < Tk; j += kAttnThreads / 32) {
         const int16_t vv = *reinterpret_cast<const int16_t *>(vb + (int64_t)j * a.ldv);
         const int32_t v0 = (int8_t)(vv & 0xFF), v1 = (int8_t)((vv >> 8) & 0xFF);
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
         int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
         v = rrs(wmul(v, inv), a.rsqrt_offset);
         v = rrs(wmul(v, (int32_t)a.av_mult), avs);
-        a.out[(int64_t)b * a.o_bs + (int64_t)(q0 + r) * a.ldo + h * 64 + d] = (int8_t)clampi(v, -127, 127);
+        a.out[(int64_t)b * a.o_bs + (int64_t)(q0 + r) * a.ldo + (int64_t)h * a.o_hs + d] = (int8_t)clampi(v, -127, 127);
     }
 }
 
@@ -531,6 +531,178 @@ cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
     }
     dim3 grid((a.Tq + kAttnQB - 1) / kAttnQB, H, B);
     attn_cc_kernel<<<grid, kAttnThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// KV-cache append (the torch.cat of Whisper_int.install_kv_cache_hooks,
+// model_int.py:1604-1610, as an in-place write into a preallocated cache).
+// ---------------------------------------------------------------------------
+__global__ void kv_append_kernel(const int8_t *__restrict__ src, int64_t lds, int k_col, int v_col,
+                                 int8_t *__restrict__ kc, int8_t *__restrict__ vc, int B, int H, int T, int Tcap,
+                                 int pos, const int32_t *pos_dev) {
+    const int p0 = pos_dev ? *pos_dev : pos;
+    const int64_t total = (int64_t)B * T * H * 16;  // int32 words per K (and per V)
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int w = (int)(i % 16);
+        const int64_t r = i / 16;
+        const int h = (int)(r % H);
+        const int64_t bt = r / H;
+        const int t = (int)(bt % T);
+        const int b = (int)(bt / T);
+        const int8_t *row = src + bt * lds;
+        const int64_t dst = (((int64_t)b * H + h) * Tcap + p0 + t) * 64 + 4 * w;
+        reinterpret_cast<int32_t *>(kc + dst)[0] = reinterpret_cast<const int32_t *>(row + k_col + h * 64)[w];
+        reinterpret_cast<int32_t *>(vc + dst)[0] = reinterpret_cast<const int32_t *>(row + v_col + h * 64)[w];
+    }
+}
+
+cudaError_t kv_append(const int8_t *src, int64_t lds, int k_col, int v_col, int8_t *kc, int8_t *vc, int B, int H,
+                      int T, int Tcap, int pos, const int32_t *pos_dev, cudaStream_t st) {
+    const int64_t total = (int64_t)B * T * H * 16;
+    if (total <= 0) return cudaSuccess;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    kv_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(src, lds, k_col, v_col, kc, vc, B, H, T, Tcap, pos, pos_dev);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// One greedy step on the device: the logit filters SuppressBlank,
+// SuppressTokens and ApplyTimestampRules (decoding.py:426-510) on the
+// dequantised logits q/alpha (model_int.py:1482-1483), then GreedyDecoder
+// (decoding.py:280-296): first index of the maximum, EOT kept once emitted.
+// One CTA per utterance.
+// ---------------------------------------------------------------------------
+static constexpr int kGreedyThreads = 1024;
+
+IW_DEV float block_reduce_max(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
+    return r;
+}
+
+IW_DEV float block_reduce_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r += red[w];
+    return r;
+}
+
+__global__ void __launch_bounds__(kGreedyThreads) greedy_step_kernel(GreedyArgs g) {
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x;
+    __shared__ float red[32];
+    __shared__ int32_t ired[32];
+    int32_t *st = g.state + 4 * b;
+    const int n = st[0], last = st[1], pen = st[2], last_ts_val = st[3];
+    const int tb = g.timestamp_begin;
+    const bool at_begin = (n == 0);
+    const bool last_ts = n >= 1 && last >= tb;
+    const bool pen_ts = n < 2 || pen >= tb;
+    int ts_hi = -1;  // timestamps in [tb, ts_hi) are forbidden
+    if (last_ts_val >= 0) ts_hi = (last_ts && !pen_ts) ? last_ts_val : last_ts_val + 1;
+    const int8_t *lg = g.logits + (int64_t)b * g.ld;
+    // masked logit value: q/alpha, -inf where a rule suppresses the token
+    auto masked_val = [&](int i) -> float {
+        if (at_begin) {
+            if (i == g.eot) return -INFINITY;
+            for (int u = 0; u < g.n_blank; ++u)
+                if (g.blank[u] == i) return -INFINITY;
+        }
+        if ((g.suppress_bits[i >> 5] >> (i & 31)) & 1u) return -INFINITY;
+        if (i == g.no_timestamps) return -INFINITY;
+        if (last_ts) {
+            if (pen_ts) {
+                if (i >= tb) return -INFINITY;
+            } else if (i < g.eot) {
+                return -INFINITY;
+            }
+        }
+        if (i >= tb && i < ts_hi) return -INFINITY;
+        if (at_begin) {
+            if (i < tb) return -INFINITY;
+            if (g.max_initial_timestamp_index >= 0 && i > tb + g.max_initial_timestamp_index) return -INFINITY;
+        }
+        return (float)lg[i] / g.alpha;
+    };
+    // log_softmax over the masked logits
+    float mx = -INFINITY;
+    for (int i = tid; i < g.V; i += kGreedyThreads) mx = fmaxf(mx, masked_val(i));
+    mx = block_reduce_max(mx, red);
+    float se = 0.f;
+    for (int i = tid; i < g.V; i += kGreedyThreads) se += expf(masked_val(i) - mx);
+    se = block_reduce_sum(se, red);
+    const float lse = logf(se);
+    // timestamp mass vs. best text token (decoding.py:500-510)
+    float m2 = -INFINITY, mt = -INFINITY;
+    for (int i = tid; i < g.V; i += kGreedyThreads) {
+        const float lp = masked_val(i) - mx - lse;
+        if (i >= tb) m2 = fmaxf(m2, lp);
+        else mt = fmaxf(mt, lp);
+    }
+    m2 = block_reduce_max(m2, red);
+    mt = block_reduce_max(mt, red);
+    float s2 = 0.f;
+    if (m2 != -INFINITY)
+        for (int i = tb + tid; i < g.V; i += kGreedyThreads) s2 += expf((masked_val(i) - mx - lse) - m2);
+    s2 = block_reduce_sum(s2, red);
+    const float ts_lp = (m2 == -INFINITY) ? -INFINITY : m2 + logf(s2);
+    const bool force_ts = ts_lp > mt;
+    // argmax (first index of the maximum)
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < g.V; i += kGreedyThreads) {
+        float v = masked_val(i);
+        if (force_ts && i < tb) v = -INFINITY;
+        if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    __syncthreads();
+    if ((tid & 31) == 0) { red[tid >> 5] = best; ired[tid >> 5] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        float bv = red[0];
+        int bidx = ired[0];
+        for (int w = 1; w < kGreedyThreads / 32; ++w)
+            if (red[w] > bv || (red[w] == bv && ired[w] < bidx)) { bv = red[w]; bidx = ired[w]; }
+        if (bidx == 0x7fffffff) bidx = 0;
+        const int col = *g.step_dev;
+        const int64_t prev = g.tokens[(int64_t)b * g.ld_tok + col - 1];
+        int64_t nxt = (prev == g.eot) ? (int64_t)g.eot : (int64_t)bidx;
+        g.tokens[(int64_t)b * g.ld_tok + col] = nxt;
+        g.next[b] = nxt;
+        st[0] = n + 1;
+        st[2] = last;
+        st[1] = (int32_t)nxt;
+        if (nxt >= tb) st[3] = (int32_t)nxt;
+    }
+}
+
+cudaError_t greedy_step(const GreedyArgs &g, int B, cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    greedy_step_kernel<<<B, kGreedyThreads, 0, st>>>(g);
+    return cudaGetLastError();
+}
+
+__global__ void add_i32_kernel(int32_t *p, int32_t v) { *p += v; }
+
+cudaError_t add_i32(int32_t *p, int32_t v, cudaStream_t st) {
+    add_i32_kernel<<<1, 1, 0, st>>>(p, v);
     return cudaGetLastError();
 }
 

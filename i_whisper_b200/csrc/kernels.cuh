@@ -25,14 +25,16 @@ struct GeluParams {
 };
 
 struct AttnArgs {
+    // element (b, t, h, d) of Q is q[b*q_bs + t*ldq + h*q_hs + d]; same for
+    // K, V and the output with their own strides (head strides default 64)
     const int8_t *q;
-    int64_t ldq, q_bs;  // row stride, batch stride (elements)
+    int64_t ldq, q_bs, q_hs = 64;
     const int8_t *k;
-    int64_t ldk, k_bs;
+    int64_t ldk, k_bs, k_hs = 64;
     const int8_t *v;
-    int64_t ldv, v_bs;
+    int64_t ldv, v_bs, v_hs = 64;
     int8_t *out;
-    int64_t ldo, o_bs;
+    int64_t ldo, o_bs, o_hs = 64;
     int Tq, Tk;
     const int32_t *Tk_dev;  // optional: key count read on the device
     int Tk_cap;             // shared-memory capacity in keys (>= any Tk)
@@ -62,6 +64,31 @@ cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K,
                    int64_t ldo, int channels_last, cudaStream_t st);
 cudaError_t pad_rows(const int8_t *x, int64_t rows, int64_t cols, int8_t *out, int64_t ldo, cudaStream_t st);
 cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st);
+
+// Append one position of self-attention K and V (row b of src, columns
+// [k_col, k_col+H*64) and [v_col, v_col+H*64)) to head-major caches
+// [B, H, Tcap, 64] at position *pos_dev (or `pos` when pos_dev is null).
+cudaError_t kv_append(const int8_t *src, int64_t lds, int k_col, int v_col, int8_t *kc, int8_t *vc, int B, int H,
+                      int T, int Tcap, int pos, const int32_t *pos_dev, cudaStream_t st);
+
+struct GreedyArgs {
+    const int8_t *logits;      // [B, V] int8 logits of the current step
+    int64_t ld;
+    int V;
+    float alpha;               // TextDecoder_int.act_logits_alpha
+    const uint32_t *suppress_bits;  // bitmap [ceil(V/32)] of SuppressTokens ids
+    const int32_t *blank;      // SuppressBlank ids (encode(" ")), eot added by the kernel
+    int n_blank;
+    int eot, timestamp_begin, no_timestamps;
+    int max_initial_timestamp_index;  // < 0: none
+    int32_t *state;            // [B, 4]: n_sampled, last, penultimate, last timestamp (-1)
+    int64_t *tokens;           // [B, ld_tok] token history; next token written at column *step_dev
+    int64_t ld_tok;
+    int32_t *step_dev;         // column of the next token (advanced by the host loop)
+    int64_t *next;             // [B] next token (also fed to the embedding gather)
+};
+cudaError_t greedy_step(const GreedyArgs &g, int B, cudaStream_t st);
+cudaError_t add_i32(int32_t *p, int32_t v, cudaStream_t st);
 cudaError_t qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, int16_t *qk, int16_t *rmax1,
                               int B, int H, int Tq, int Tk, int D, uint8_t mult, int32_t shift, cudaStream_t st);
 cudaError_t shift_exp(const int16_t *x, const int16_t *rmax1, const uint8_t *mask, uint8_t *p, int32_t *rowsum, int B,

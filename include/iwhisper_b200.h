@@ -160,6 +160,131 @@ int iw_classifier(const int8_t *x, const int8_t *weight, uint32_t multiplier, in
  * zero-point term, linear.py:89-91). */
 int iw_rowsum_i8(const int8_t *x, int64_t ldx, int64_t M, int64_t K, int32_t *y, void *stream);
 
+
+/* ------------------------------------------------------------------------
+ * Model-level entry points. They expose the fused forms the B200 runner
+ * uses for Whisper_int.forward (model_int.py:1064-1484): GEMMs with the
+ * requantisation, GeLU, Residual15, positional add and cache layouts in
+ * their epilogues, attention over strided projections and head-major
+ * caches, and device-side decode state so a decode step can be captured in
+ * a CUDA graph and replayed.
+ * ---------------------------------------------------------------------- */
+
+/* Epilogue modes of iw_gemm_i8. */
+#define IW_GEMM_ACC32 0       /* int32: acc + bias - wz*rowsum                  */
+#define IW_GEMM_INT8 1        /* int8: Linear8 / conv / classifier requant      */
+#define IW_GEMM_LINEAR32 2    /* int32: Linear32 requant                        */
+#define IW_GEMM_LINEAR32_RES 3 /* int16: Linear32 requant + residual15          */
+
+typedef struct iw_gemm_desc {
+    const int8_t *x;          /* [M,K], row stride ldx bytes (multiple of 16)  */
+    int64_t ldx;
+    const int8_t *w;          /* [N,K], row stride ldw bytes (multiple of 16)  */
+    int64_t ldw;
+    int64_t M, N, K;          /* K multiple of 16 */
+    int mode;                 /* IW_GEMM_* */
+    void *out;
+    int64_t ldo;              /* output row stride in elements */
+    const int32_t *bias;      /* [N]? */
+    const int8_t *weight_zero;/* [N]? (needs x_rowsum) */
+    const int32_t *x_rowsum;  /* [M] sum of each x row */
+    const uint32_t *multiplier; /* [N] per channel, or NULL for the scalar pair */
+    const int8_t *shift;        /* [N] */
+    uint32_t scalar_multiplier;  /* conv1d / classifier requant */
+    int32_t scalar_shift;        /* used as max(shift, 0) */
+    /* GeLU on the int8 result (gelu_scalar.cpp), lut != NULL enables it */
+    const uint8_t *lut;
+    const uint8_t *luti_multiplier;
+    const int8_t *luti_shift;
+    const uint8_t *luto_multiplier;
+    const int8_t *luto_shift;
+    int luti_per_channel, luto_per_channel;
+    /* Residual15 for IW_GEMM_LINEAR32_RES: out = residual15(y, residual, m) */
+    const int16_t *residual;
+    int64_t ldr;
+    uint32_t residual_multiplier;
+    /* positional add + requant to INT15 (add_requant15_scalar.cpp) on the
+     * int8 result: pos != NULL makes the output int16; row m uses position
+     * m % pos_T of pos [pos_T, N]; multiplier/shift per channel or scalar */
+    const int8_t *pos;
+    int64_t pos_T;
+    const uint16_t *pos_multiplier;
+    const int8_t *pos_shift;
+    int pos_per_channel;
+    /* alternative int8 output layouts (0 = row-major [M,N]) */
+    int64_t transpose_T;      /* out [B,N,T] with m = b*T + t                  */
+    int64_t headmajor_T;      /* out [N/64, B, T, 64] with m = b*T + t          */
+    int64_t headmajor_B;
+    int32_t *out_rowsum;      /* [M]? accumulate row sums of the int8 output    */
+    int tile_n;               /* 0 = automatic, else 64/128/256 */
+} iw_gemm_desc;
+
+/* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */
+int iw_gemm_i8(const iw_gemm_desc *d, void *stream);
+
+typedef struct iw_attn_desc {
+    /* element (b,t,h,d) of Q is q[b*q_bs + t*ldq + h*q_hs + d], same for
+     * K, V and the output y; head_dim is 64 */
+    const int8_t *q; int64_t ldq, q_bs, q_hs;
+    const int8_t *k; int64_t ldk, k_bs, k_hs;
+    const int8_t *v; int64_t ldv, v_bs, v_hs;
+    int8_t *y; int64_t ldy, y_bs, y_hs;
+    int64_t B, H, Tq, Tk;
+    const int32_t *Tk_dev;    /* optional: key count read on the device       */
+    int64_t Tk_cap;           /* upper bound of *Tk_dev                        */
+    int mask_mode;            /* 0 none, 1 causal, 2 explicit [Tq,Tk]          */
+    const uint8_t *mask;
+    uint8_t qk_multiplier; int8_t qk_shift; int32_t frac_bits;
+    uint8_t av_multiplier; int8_t av_shift; int32_t rsqrt_offset;
+} iw_attn_desc;
+
+int iw_attention_ex(const iw_attn_desc *d, void *stream);
+
+/* LayerNorm32 over rows with strides; optionally writes the row sums of the
+ * int8 output (rowsum_out) and zeroes rowsum_zero[rows] for a later
+ * accumulating epilogue. */
+int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
+                      uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
+                      int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream);
+
+/* im2col of the conv stem: row (b,t), column cin*K+k = x[b,cin,t*stride-pad+k]
+ * (channels_last: x[b,t',cin]), zero outside; out row stride ldo >= Cin*K. */
+int iw_im2col(const int8_t *x, int8_t *out, int64_t B, int64_t Cin, int64_t Tin, int64_t K, int64_t stride,
+              int64_t pad, int64_t Tout, int64_t ldo, int channels_last, void *stream);
+
+/* Embedding gather + add_requant15 with the position offset read from the
+ * device (*offset_dev) when offset_dev != NULL. */
+int iw_embed_add_requant15_dev(const int8_t *table, const int64_t *tokens, const int8_t *pe,
+                               const int32_t *offset_dev, int64_t offset, const uint16_t *multiplier,
+                               const int8_t *shift, int16_t *y, int64_t B, int64_t T, int64_t C,
+                               int64_t multiplier_count, int64_t shift_count, void *stream);
+
+/* Write T positions of K and V (columns k_col.., v_col.. of the rows of
+ * src [B*T, lds]) into head-major caches [B,H,Tcap,64] at position
+ * *pos_dev (or pos). Replaces the torch.cat KV hooks of
+ * Whisper_int.install_kv_cache_hooks (model_int.py:1587-1618). */
+int iw_kv_append(const int8_t *src, int64_t lds, int64_t k_col, int64_t v_col, int8_t *k_cache, int8_t *v_cache,
+                 int64_t B, int64_t H, int64_t T, int64_t Tcap, int64_t pos, const int32_t *pos_dev, void *stream);
+
+typedef struct iw_greedy_desc {
+    const int8_t *logits; int64_t ld; int64_t V;
+    float alpha;
+    const uint32_t *suppress_bits; const int32_t *blank; int64_t n_blank;
+    int64_t eot, timestamp_begin, no_timestamps, max_initial_timestamp_index;
+    int32_t *state;           /* [B,4] n_sampled, last, penultimate, last timestamp */
+    int64_t *tokens; int64_t ld_tok;
+    int32_t *step_dev;        /* column of the next token in tokens */
+    int64_t *next;            /* [B] */
+} iw_greedy_desc;
+
+/* One greedy decoding step on the device: SuppressBlank, SuppressTokens,
+ * ApplyTimestampRules (decoding.py:426-510) and GreedyDecoder.update
+ * (decoding.py:280-296). */
+int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream);
+
+/* *p += v on the device (advances device-side decode counters). */
+int iw_add_i32(int32_t *p, int32_t v, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,77 @@
+"""Model-level parity on the GPU: WhisperIntB200 (encoder + greedy decoder)
+against the reference golden fixture and against the oracle dataflow."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from i_whisper_b200.checkpoint import ModelDims, synthetic_state_dict
+from i_whisper_b200.model import decode_tokens
+from i_whisper_b200.synthetic import synthetic_mel_batch
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "model_golden.json")
+
+
+def sha(a):
+    if isinstance(a, torch.Tensor):
+        a = a.cpu().numpy()
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def decode_spec(n_vocab):
+    t = decode_tokens(n_vocab)
+    return O.DecodeTokens(sot=t["sot"], eot=t["eot"], sot_sequence=t["sot_sequence"], no_timestamps=t["no_timestamps"],
+                          timestamp_begin=t["timestamp_begin"], blank=t["blank"], suppress=t["suppress"])
+
+
+@pytest.mark.parametrize("case", list(json.load(open(GOLDEN))))
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_model_matches_reference_golden(case, use_graph):
+    from i_whisper_b200.model import WhisperIntB200
+    g = json.load(open(GOLDEN))[case]
+    dims = ModelDims(**g["dims"])
+    sd = synthetic_state_dict(dims, g["seed"])
+    mel = synthetic_mel_batch(dims.n_mels, g["mel_seeds"], float(sd["encoder.input_alpha"][0]))
+    model = WhisperIntB200(dims, sd)
+    trace = {}
+    xa = model.encoder(torch.from_numpy(mel).cuda(), trace=trace)
+    for k, h in enumerate(g["block_sha256"]):
+        assert sha(trace[f"encoder.blocks.{k}"].reshape(len(g["mel_seeds"]), dims.n_audio_ctx, -1)) == h, f"block {k}"
+    assert sha(xa) == g["encoder_sha256"]
+    toks = model.decode(xa, model._enc_ws[xa.shape[0]]["rs_xa"], g["sample_len"], use_graph=use_graph)
+    ref = g["tokens"]
+    assert toks.cpu().tolist() == ref
+
+
+CASES = [
+    # (dims, seed, mel seeds, decode steps)
+    (ModelDims(80, 1500, 384, 6, 2, 51865, 448, 384, 6, 2), 3, [5, 6], 12),
+    (ModelDims(80, 1500, 512, 8, 1, 51865, 448, 512, 8, 1), 4, [7], 10),
+    (ModelDims(80, 1500, 768, 12, 1, 51865, 448, 768, 12, 1), 5, [8], 6),
+    (ModelDims(128, 1500, 1280, 20, 1, 51866, 448, 1280, 20, 1), 6, [9], 6),
+]
+
+
+@pytest.mark.parametrize("dims,seed,mel_seeds,steps", CASES)
+def test_model_matches_oracle(dims, seed, mel_seeds, steps):
+    from i_whisper_b200.model import WhisperIntB200
+    sd = synthetic_state_dict(dims, seed)
+    mel = synthetic_mel_batch(dims.n_mels, mel_seeds, float(sd["encoder.input_alpha"][0]))
+    odims = O.Dims(**dims.__dict__)
+    xa_ref = O.encoder_forward(sd, odims, mel)
+    model = WhisperIntB200(dims, sd)
+    xa = model.encoder(torch.from_numpy(mel).cuda())
+    assert np.array_equal(xa.cpu().numpy(), xa_ref)
+    ref = O.greedy_decode(sd, odims, xa_ref, decode_spec(dims.n_vocab), steps, stop_when_done=False)
+    toks = model.decode(xa, model._enc_ws[xa.shape[0]]["rs_xa"], steps, use_graph=True)
+    assert toks.cpu().numpy().tolist() == ref.tolist()
+
+
+def test_device_status_clean_after_model():
+    from i_whisper_b200 import _lib
+    assert _lib.device_status(clear=True) == 0
