@@ -1,0 +1,442 @@
+"""Benchmark of the B200 integer Whisper path (the repository's bench contract).
+
+Workload (per GPU): whisper-medium integer encoder
+over a batch of 256 synthetic 30 s windows (d_model 1024, 24 layers, 16
+heads, 80 mels), then greedy decoding of 128 tokens per window with an INT8
+self-attention KV cache and INT8 cross-attention over the 1500 encoder
+states. Weights are the deterministic synthetic checkpoint
+(``checkpoint.synthetic_state_dict``, seed 0); inputs are seeded sine+noise
+windows through the float log-mel frontend (seeds recycled modulo 32).
+
+* ``value``: encoder windows/s of the whole job (all ranks), inputs resident
+  in HBM; one step = one encoder pass over the batch.
+* ``e2e``: the same metric through the public API with host buffers: each
+  step copies the INT8 mel batch from pinned host memory, runs the encoder
+  and reads the INT8 features back to pinned host memory.
+* ``decoder``: greedy decoding tok/s (device-resident and end to end with
+  the token matrix read back).
+* ``roofline``: the dominant kernel, achieved work per launch from CUDA
+  events over the timed steps.
+* ``cpu_baseline``: the reference's own scalar C++ kernels (oracle/_ref) on a
+  bounded sample of the same workload on the host cores (rank 0, N=1).
+
+Multi-GPU: one process per GPU (torchrun); utterances are sharded by
+rank with no collective on the data path; ``scaling`` is weak (each rank
+owns a fixed batch). ``--impl reference`` times the reference CPU path
+instead (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8 encoder 30s-windows/sec (whisper-medium) + % int8 TC peak; decoder tok/s"
+DATASHEET_INT8_TOPS = 4500.0
+ENC_GOP = {"tiny": 36.9, "small": 344.2, "medium": 1138.1, "large": 2273.8}
+
+
+def enc_gop(d):
+    """Algorithmic encoder work per window (QK^T counted once):
+    L*(24*T*d^2 + 4*T^2*d) + 2*(3000*3*n_mels*d + 1500*3*d^2), in GOP."""
+    T = d.n_audio_ctx
+    L, dm, nm = d.n_audio_layer, d.n_audio_state, d.n_mels
+    return (L * (24 * T * dm * dm + 4 * T * T * dm) + 2 * (2 * T * 3 * nm * dm + T * 3 * dm * dm)) / 1e9
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="medium")
+    ap.add_argument("--batch", type=int, default=256, help="windows per GPU")
+    ap.add_argument("--decode-tokens", type=int, default=128)
+    ap.add_argument("--decode-runs", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-rows", type=int, default=64, help="query rows of the CPU sample")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU reference timing (bounded samples of the same workload)
+# ---------------------------------------------------------------------------
+def _cpu_sample_worker(args):
+    """One process: time one medium encoder layer + stem on `rows` of the
+    1500 positions, and one decoder step (1 layer + classifier), with the
+    chosen kernel library; returns seconds."""
+    kind, rows, seed, model = args
+    from oracle import oracle as O
+    from i_whisper_b200.checkpoint import DIMS
+    L = O.lib(kind)
+    if kind == "port":
+        L.set_threads(1)
+    dims = DIMS[model]
+    d, H, T = dims.n_audio_state, dims.n_audio_head, dims.n_audio_ctx
+    rng = np.random.default_rng(seed)
+    i8 = lambda *s: rng.integers(-60, 61, s, dtype=np.int8)
+    lin = lambda n_in, n_out: (i8(n_out, n_in), rng.integers(-1000, 1000, n_out, dtype=np.int32),
+                               rng.integers(-4, 5, n_out).astype(np.int8),
+                               rng.integers(2 ** 30, 2 ** 31, n_out, dtype=np.uint32),
+                               np.full(n_out, 12, np.int8))
+    wq, wk, wv, wo, w1, w2 = lin(d, d), lin(d, d), lin(d, d), lin(d, d), lin(d, 4 * d), lin(4 * d, d)
+    x16 = rng.integers(-3000, 3000, (rows, d), dtype=np.int16)
+    g = rng.integers(40, 90, d, dtype=np.int8)
+    be = rng.integers(-1000, 1000, d, dtype=np.int32)
+    kfull = i8(1, H, T, 64)
+    vtfull = i8(1, H, 64, T)
+    lut = np.arange(16, dtype=np.uint8) * 16
+    mi, si = np.ones(4 * d, np.uint8), np.full(4 * d, 4, np.int8)
+    mo, so = np.full(4 * d, 128, np.uint8), np.full(4 * d, 15, np.int8)
+    mel = i8(1, dims.n_mels, 2 * rows + 2)
+    wc1, wc2 = i8(d, dims.n_mels * 3), i8(d, 3 * d)
+
+    def layer():
+        h = L.layernorm32(x16, g, be, 128, 9, 2 ** 30, 10)
+        q = L.linear8(h, *wq); L.linear8(h, *wk); L.linear8(h, *wv)
+        q4 = np.ascontiguousarray(q.reshape(1, rows, H, 64).transpose(0, 2, 1, 3))
+        s, rm = L.qk_requant_rowmax(q4, kfull, None, 182, 12)
+        p, rs = L.shift_exp(s, rm, None, 7)
+        a = L.pv_norm_requant(p, vtfull, rs, 192, 7, 16).reshape(rows, d)
+        x = L.residual15(L.linear32(a, *wo), x16, 31130)
+        h = L.layernorm32(x, g, be, 128, 9, 2 ** 30, 10)
+        f = L.gelu(L.linear8(h, *w1), lut, mi, si, mo, so)
+        L.residual15(L.linear32(f, *w2), x, 31130)
+
+    def stem():
+        y = L.conv1d(mel, wc1, None, 2 ** 30, 10, 1, 1)
+        L.conv1d(y, wc2, None, 2 ** 30, 10, 2, 1)
+
+    t0 = time.perf_counter(); layer(); t_layer = time.perf_counter() - t0
+    t0 = time.perf_counter(); stem(); t_stem = time.perf_counter() - t0
+    # one decoder step of one utterance: 1 layer (self Tk 67, cross Tk 1500) + classifier
+    x1 = x16[:1]
+    ks, vts = i8(1, H, 67, 64), i8(1, H, 64, 67)
+    emb = i8(dims.n_vocab, d)
+
+    def dec_layer():
+        h = L.layernorm32(x1, g, be, 128, 9, 2 ** 30, 10)
+        q = L.linear8(h, *wq); L.linear8(h, *wk); L.linear8(h, *wv)
+        q4 = np.ascontiguousarray(q.reshape(1, 1, H, 64).transpose(0, 2, 1, 3))
+        for kk, vv in ((ks, vts), (kfull, vtfull)):
+            s, rm = L.qk_requant_rowmax(q4, kk, None, 182, 12)
+            p, rs = L.shift_exp(s, rm, None, 7)
+            a = L.pv_norm_requant(p, vv, rs, 192, 7, 16).reshape(1, d)
+            x = L.residual15(L.linear32(a, *wo), x1, 31130)
+            L.linear8(L.layernorm32(x, g, be, 128, 9, 2 ** 30, 10), *wq)
+        f = L.gelu(L.linear8(h, *w1), lut, mi, si, mo, so)
+        L.residual15(L.linear32(f, *w2), x, 31130)
+
+    t0 = time.perf_counter(); dec_layer(); t_dec_layer = time.perf_counter() - t0
+    t0 = time.perf_counter(); L.classifier(L.layernorm32(x1, g, be, 128, 9, 2 ** 30, 10), emb, 2 ** 30, 10)
+    t_clf = time.perf_counter() - t0
+    return t_layer, t_stem, t_dec_layer, t_clf
+
+
+def cpu_baseline(model: str, rows: int, procs: int):
+    """Reference CPU throughput from bounded samples: `procs` single-threaded
+    processes (spawned) each time one sampled encoder layer + stem and one
+    decoder step; per-window time = 24 layers x (1500/rows) x layer sample +
+    stem scaled the same way. Returns (windows/s, tok/s, kind, cores, sample)."""
+    import multiprocessing as mp
+    from oracle import oracle as O
+    from i_whisper_b200.checkpoint import DIMS
+    kind = "reference" if os.path.exists(O.REF_PATH) else "port"
+    lib_kind = "ref" if kind == "reference" else "port"
+    dims = DIMS[model]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_cpu_sample_worker, [(lib_kind, rows, 1000 + i, model) for i in range(procs)])
+    t_layer = float(np.mean([r[0] for r in res]))
+    t_stem = float(np.mean([r[1] for r in res]))
+    t_dec = float(np.mean([r[2] for r in res]))
+    t_clf = float(np.mean([r[3] for r in res]))
+    scale = dims.n_audio_ctx / rows
+    t_window = dims.n_audio_layer * t_layer * scale + t_stem * scale
+    t_token = dims.n_text_layer * t_dec + t_clf
+    sample = (f"{procs} processes x (1 encoder layer + conv stem on {rows}/{dims.n_audio_ctx} positions, "
+              f"1 decoder layer step + classifier for 1 utterance); per-window time extrapolated x{scale:.1f} rows "
+              f"x{dims.n_audio_layer} layers")
+    return procs / t_window, procs / t_token, kind, procs, sample
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    def __init__(self, dev_index: int):
+        self.dev = dev_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def int8_mm_peak(torch):
+    """Empirical dense INT8 tensor-core ceiling: torch._int_mm (cuBLASLt
+    IMMA) on 8192^3, best of 10 (burst)."""
+    a = torch.randint(-100, 100, (8192, 8192), dtype=torch.int8, device="cuda")
+    b = torch.randint(-100, 100, (8192, 8192), dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = 1e9
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); torch._int_mm(a, b); e1.record(); e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p))
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from i_whisper_b200.checkpoint import DIMS, synthetic_state_dict
+    from i_whisper_b200.model import KernelTimer, WhisperIntB200
+    from i_whisper_b200.synthetic import synthetic_mel_batch
+
+    # CPU baseline processes are spawned before this process touches the GPU
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.model, args.cpu_rows, os.cpu_count() or 1)
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            t = torch.ones(1, device="cuda")
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+
+    dims = DIMS[args.model]
+    B = args.batch
+    sd = synthetic_state_dict(dims, seed=0)
+    model = WhisperIntB200(dims, sd)
+    del sd
+    seeds = [(rank * B + i) % 32 for i in range(B)]
+    mels32 = synthetic_mel_batch(dims.n_mels, sorted(set(seeds)), 100.0)
+    mel_np = np.stack([mels32[s % len(mels32)] for s in seeds])
+    mel = torch.from_numpy(mel_np).cuda()
+    enc_gops = enc_gop(dims)
+
+    # ---- encoder, device-resident inputs ---------------------------------
+    for _ in range(args.warmup):
+        model.encoder(mel)
+    barrier()
+    timer = KernelTimer()
+    model.timer = timer
+    launches0 = model.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record()
+        for _ in range(args.steps):
+            model.encoder(mel)
+        e1.record()
+        barrier()
+    model.timer = None
+    enc_ms = e0.elapsed_time(e1)
+    launches = (model.launches - launches0)
+    ksum = timer.summary()
+    t_max = torch.tensor([enc_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    enc_ms = float(t_max.item())
+    windows = B * world * args.steps
+    value = windows / (enc_ms / 1e3)
+    ms_per_step = enc_ms / args.steps
+
+    # ---- encoder end to end through the public API (host buffers) ----------
+    h_mel = torch.from_numpy(mel_np).pin_memory()
+    h_out = torch.empty(B, dims.n_audio_ctx, dims.n_audio_state, dtype=torch.int8).pin_memory()
+    for _ in range(1):
+        xa = model.encoder(h_mel.cuda(non_blocking=True))
+        h_out.copy_(xa, non_blocking=True)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        d_mel = h_mel.cuda(non_blocking=True)
+        xa = model.encoder(d_mel)
+        h_out.copy_(xa, non_blocking=True)
+    f1.record()
+    barrier()
+    e2e_ms = torch.tensor([f0.elapsed_time(f1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = windows / (float(e2e_ms.item()) / 1e3)
+
+    # ---- greedy decoder ------------------------------------------------------
+    xa = model.encoder(mel)
+    rs_xa = model._enc_ws[B]["rs_xa"]
+    model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)  # warm-up + graph capture
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(args.decode_runs):
+        toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
+    g1.record()
+    barrier()
+    dec_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(dec_ms, op=dist.ReduceOp.MAX)
+    dec_tokens = B * world * args.decode_tokens * args.decode_runs
+    dec_tps = dec_tokens / (float(dec_ms.item()) / 1e3)
+    h_tok = torch.empty(B, 3 + args.decode_tokens, dtype=torch.int64).pin_memory()
+    g0.record()
+    toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
+    h_tok.copy_(toks, non_blocking=True)
+    g1.record()
+    barrier()
+    dec_e2e_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
+    if world > 1:
+        dist.all_reduce(dec_e2e_ms, op=dist.ReduceOp.MAX)
+    dec_e2e_tps = B * world * args.decode_tokens / (float(dec_e2e_ms.item()) / 1e3)
+
+    # ---- roofline of the dominant kernel ------------------------------------
+    peaks = measured_peaks()
+    int8_peak = int8_mm_peak(torch)
+    dom = max(ksum.items(), key=lambda kv: kv[1]["ms"])
+    dname, dk = dom
+    kernels = {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                   "share": round(v["ms"] / max(1e-9, sum(x["ms"] for x in ksum.values())), 4),
+                   "tops": round(v["ops"] / (v["ms"] * 1e-3) / 1e12, 2) if v["ops"] else None}
+               for k, v in ksum.items()}
+    if dk["ops"]:
+        achieved = dk["ops"] / dk["launches"] / (dk["ms"] / dk["launches"] * 1e-3) / 1e12
+        roof = {"kernel": dname, "bound": "tensor", "achieved": round(achieved, 2), "peak": round(int8_peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4),
+                "peak_source": "measured torch._int_mm int8 8192^3 burst on this GPU (no INT8 entry in MEASURED_PEAKS.json)",
+                "frac_of_datasheet_4500": round(achieved / DATASHEET_INT8_TOPS, 4),
+                "traffic": None, "algorithmic_ops_per_launch": dk["ops"] / dk["launches"]}
+    else:
+        achieved = dk["bytes"] / dk["launches"] / (dk["ms"] / dk["launches"] * 1e-3) / 1e9
+        roof = {"kernel": dname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None}
+    enc_tops = enc_gops * B * args.steps / (ms_per_step * args.steps * 1e-3) / 1e3
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "windows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded sine+noise windows; random-init synthetic checkpoint)",
+        "config": {"workload": f"whisper-{args.model} integer encoder, {B} windows per GPU (BASELINE configs[3]); "
+                               f"greedy decoder {args.decode_tokens} tokens", "model": f"whisper-{args.model}",
+                   "global_batch": B * world, "seq_len": dims.n_audio_ctx, "parallelism": f"utterance-sharded x{world}",
+                   "l2": "working set per step > 5 GB (inputs larger than L2)"},
+        "pct_int8_tc_peak": {"encoder_tops": round(enc_tops, 1),
+                             "of_measured_int8_mm": round(enc_tops / int8_peak, 4),
+                             "of_datasheet_4500": round(enc_tops / DATASHEET_INT8_TOPS, 4)},
+        "decoder": {"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
+                    "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
+                    "ms_per_decode": round(float(dec_ms.item()) / args.decode_runs, 2)},
+        "e2e": {"value": round(e2e_value, 3), "unit": "windows/s", "h2d_bytes_per_step": int(h_mel.numel()),
+                "d2h_bytes_per_step": int(h_out.numel())},
+        "roofline": roof,
+        "kernels": kernels,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        cw, ct, kind, cores, sample = cpu
+        line["cpu_baseline"] = {"value": round(cw, 6), "unit": "windows/s", "cores": cores, "kind": kind,
+                                "sample": sample, "decoder_tok_per_s": round(ct, 3)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    procs = os.cpu_count() or 1
+    t0 = time.time()
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(args.model, args.cpu_rows, procs)
+    t_start = time.time()
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(args.model, args.cpu_rows, procs))
+    wall = time.time() - t_start
+    cw = float(np.mean([v[0] for v in vals]))
+    ct = float(np.mean([v[1] for v in vals]))
+    kind, cores, sample = vals[0][2], vals[0][3], vals[0][4]
+    line = {"impl": "reference", "metric": METRIC, "value": round(cw, 6), "unit": "windows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / cw, 1) if cw else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "config": {"workload": f"whisper-{args.model} integer encoder (reference CPU kernels)",
+                                            "model": f"whisper-{args.model}"},
+            "decoder": {"tok_per_s": round(ct, 4)},
+            "cpu_baseline": {"value": round(cw, 6), "unit": "windows/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": round(cw, 6), "unit": "windows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": round(wall + 0 * t0, 1)}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

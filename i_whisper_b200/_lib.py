@@ -53,6 +53,7 @@ SIGNATURES = {
     "iw_kv_append": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "iw_greedy_step": [_P, _I64, _P],
     "iw_add_i32": [_P, _I32, _P],
+    "iw_gelu_table": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
 }
 
 IW_GEMM_ACC32, IW_GEMM_INT8, IW_GEMM_LINEAR32, IW_GEMM_LINEAR32_RES = 0, 1, 2, 3
@@ -70,7 +71,7 @@ class GemmDesc(C.Structure):
         ("residual", _P), ("ldr", _I64), ("residual_multiplier", _U32),
         ("pos", _P), ("pos_T", _I64), ("pos_multiplier", _P), ("pos_shift", _P), ("pos_per_channel", C.c_int),
         ("transpose_T", _I64), ("headmajor_T", _I64), ("headmajor_B", _I64),
-        ("out_rowsum", _P), ("tile_n", C.c_int),
+        ("out_rowsum", _P), ("tile_n", C.c_int), ("gelu_table", _P),
     ]
 
 

@@ -209,7 +209,9 @@ def synthetic_state_dict(dims: ModelDims, seed: int = 0) -> Dict[str, np.ndarray
     act = 30.0
 
     def weights(key, shape, std=40.0):
-        sd[key] = np.clip(np.rint(_rng(seed, key).normal(0, std, shape)), -127, 127).astype(np.int8)
+        # uniform integers in [-h, h] with standard deviation ~std
+        h = int(round(np.sqrt(3.0) * std))
+        sd[key] = _rng(seed, key).integers(-h, h + 1, shape, dtype=np.int8)
 
     def linear8(pre, n_in, n_out, bias=True, out_std=act):
         weights(pre + ".weight", (n_out, n_in))

@@ -412,8 +412,22 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     p.hm_T = (int)d->headmajor_T;
     p.hm_B = (int)d->headmajor_B;
     p.rowsum_out = d->out_rowsum;
+    p.gelu_tab = d->gelu_table;
+    if (d->gelu_table && (d->lut || d->mode != IW_GEMM_INT8 || !d->multiplier))
+        return fail(IW_EINVAL, "iw_gemm_i8: gelu_table needs a per-channel int8 epilogue without lut");
     iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
     return cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8");
+}
+
+int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,
+                  const uint8_t *luto_multiplier, const int8_t *luto_shift, int64_t luti_count, int64_t luto_count,
+                  int64_t N, int8_t *table, void *stream) {
+    if (N <= 0) return fail(IW_EINVAL, "iw_gelu_table: N must be positive");
+    if (!(luti_count == 1 || luti_count == N) || !(luto_count == 1 || luto_count == N))
+        return fail(IW_EINVAL, "iw_gelu_table: parameter counts must be 1 or N");
+    return cuda_check(iw::gelu_table_build(lut, luti_multiplier, luti_shift, luto_multiplier, luto_shift,
+                                           (int)luti_count, (int)luto_count, (int)N, table, S(stream)),
+                      "iw_gelu_table");
 }
 
 int iw_attention_ex(const iw_attn_desc *d, void *stream) {

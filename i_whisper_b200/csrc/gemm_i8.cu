@@ -35,14 +35,21 @@ static constexpr int kBlockK = 128;  // bytes = int8 elements per k-block (one s
 static constexpr int kEpiWarps = 8;
 static constexpr int kThreads = 64 + 32 * kEpiWarps;
 
-template <int BN>
+// FLAVOR 0: general epilogue (any EpiParams); 1: fast per-channel epilogue
+// with column parameters staged in shared memory; 2: fast + GeLU table.
+template <int BN, int FLAVOR>
 struct GemmCfg {
-    static constexpr int STAGES = BN >= 256 ? 4 : 6;
     static constexpr int A_BYTES = kBlockM * kBlockK;
     static constexpr int B_BYTES = BN * kBlockK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int PARAM_BYTES = FLAVOR ? BN * 32 : 0;
+    static constexpr int GTAB_BYTES = FLAVOR == 2 ? BN * 256 : 0;
+    static constexpr int FIXED = 1024 + 256 + PARAM_BYTES + GTAB_BYTES;
+    static constexpr int STAGES_FIT = (232448 - FIXED) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+    static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
+    static_assert(STAGES >= 2, "shared memory too small");
 };
 
 IW_DEV int32_t requant32(int32_t v, uint32_t m, int8_t s) {
@@ -226,11 +233,109 @@ IW_DEV void epi_chunk(const EpiParams &p, int m, int n0, const uint32_t (&acc)[3
     }
 }
 
-template <int BN, int MODE>
+
+// ---------------------------------------------------------------------------
+// Fast epilogue: per-column constants precomputed once per tile into shared
+// memory so that the per-element requantisation is branch-free:
+//   A = {bias, -weight_zero, multiplier (as int32), multiplier >= 2^31 ? -1 : 0}
+//   Linear8:  B = {2^(s-1) or 0, s in [1,31] ? -1 : 0, s (or 0), s < 32 ? -1 : 0}
+//   Linear32: B = {s (or 0), s < 32 ? -1 : 0, 0, 0}
+// with s the shift as uint32 (negative int8 shifts are >= 32).
+// mulh(a, m) = mulhi_signed(a, (int32)m) + (m >= 2^31 ? a : 0).
+// ---------------------------------------------------------------------------
+template <int BN, int MODE, int FLAVOR>
+IW_DEV void stage_columns(const EpiParams &p, int n0, int N, int4 *colA, int4 *colB, int8_t *gtab, int et) {
+    for (int c = et; c < BN; c += kEpiWarps * 32) {
+        const int n = n0 + c;
+        int4 a = make_int4(0, 0, 0, 0), b = make_int4(0, 0, 0, 0);
+        if (n < N) {
+            const uint32_t m = p.mult[n];
+            const uint32_t sh = (uint32_t)(int32_t)p.shift[n];
+            a = make_int4(p.bias ? p.bias[n] : 0, p.wz ? -(int32_t)p.wz[n] : 0, (int32_t)m, (m >> 31) ? -1 : 0);
+            if (MODE == EPI_L8) {
+                if (sh == 0) b = make_int4(0, 0, 0, -1);
+                else if (sh < 32) b = make_int4((int32_t)(1u << (sh - 1)), -1, (int32_t)sh, -1);
+            } else {
+                if (sh < 32) b = make_int4((int32_t)sh, -1, 0, 0);
+            }
+        }
+        colA[c] = a;
+        colB[c] = b;
+    }
+    if (FLAVOR == 2) {
+        const int rows = min(BN, N - n0);
+        const int4 *src = reinterpret_cast<const int4 *>(p.gelu_tab + (int64_t)n0 * 256);
+        int4 *dst = reinterpret_cast<int4 *>(gtab);
+        for (int i = et; i < rows * 16; i += kEpiWarps * 32) dst[i] = __ldg(src + i);
+    }
+}
+
+IW_DEV void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
+
+IW_DEV int32_t u_add(int32_t a, int32_t b) { return (int32_t)((uint32_t)a + (uint32_t)b); }
+IW_DEV int32_t u_mad(int32_t a, int32_t b, int32_t c) { return (int32_t)((uint32_t)a * (uint32_t)b + (uint32_t)c); }
+
+// One 32-column chunk of row m, fast path. Returns the sum of the int8
+// outputs (Linear8) for the optional row-sum output.
+template <int MODE, int FLAVOR>
+IW_DEV int32_t epi_fast_chunk(const EpiParams &p, int m, int nc, int cl, int32_t rs, const uint32_t (&acc)[32],
+                              const int4 *colA, const int4 *colB, const int8_t *gtab, int8_t *out8) {
+    int32_t osum = 0;
+    if constexpr (MODE == EPI_L8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int4 A = colA[cl + j];
+            const int4 Bv = colB[cl + j];
+            int32_t a = u_mad(A.y, rs, u_add((int32_t)acc[j], A.x));
+            const int32_t h = u_add(__mulhi(a, A.z), a & A.w);
+            int32_t t = u_add(u_add(h, Bv.x), (h >> 31) & Bv.y);
+            t = (t >> Bv.z) & Bv.w;
+            t = clampi(t, -127, 127);
+            if constexpr (FLAVOR == 2) t = gtab[(cl + j) * 256 + t + 128];
+            osum += t;
+            if ((j & 3) == 0) w[j >> 2] = 0;
+            w[j >> 2] |= (uint32_t)(uint8_t)t << (8 * (j & 3));
+        }
+        *reinterpret_cast<uint4 *>(out8) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(out8 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {  // EPI_L32_RES
+        int16_t *out = reinterpret_cast<int16_t *>(p.out) + (int64_t)m * p.ldo + nc;
+        const int16_t *res = p.res + (int64_t)m * p.ldr + nc;
+        uint32_t r[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(res + 8 * q);
+            r[4 * q] = t.x; r[4 * q + 1] = t.y; r[4 * q + 2] = t.z; r[4 * q + 3] = t.w;
+        }
+        uint32_t o[16];
+        const int32_t rm = (int32_t)p.res_mult;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int4 A = colA[cl + j];
+            const int4 Bv = colB[cl + j];
+            int32_t a = u_mad(A.y, rs, u_add((int32_t)acc[j], A.x));
+            const int32_t h = u_add(__mulhi(a, A.z), a & A.w);
+            const int32_t br = (int32_t)((uint32_t)h << Bv.x) & Bv.y;
+            const int32_t rv = (int32_t)(int16_t)((r[j >> 1] >> (16 * (j & 1))) & 0xFFFF);
+            int32_t v = u_mad(rv, rm, br);
+            v = u_add(u_add(v, 1 << 14), v >> 31) >> 15;
+            v = clampi(v, -16383, 16383);
+            if ((j & 1) == 0) o[j >> 1] = 0;
+            o[j >> 1] |= (uint32_t)(uint16_t)v << (16 * (j & 1));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4 *>(out + 8 * q) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+    }
+    return osum;
+}
+
+template <int BN, int MODE, int FLAVOR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, const EpiParams p) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, FLAVOR>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -243,6 +348,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *drain = tempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile uint32_t *abort_flag = tmem_slot + 1;
+    int4 *colA = reinterpret_cast<int4 *>(smem + S * Cfg::STAGE_BYTES + 256);
+    int4 *colB = colA + BN;
+    int8_t *gtab = reinterpret_cast<int8_t *>(smem + S * Cfg::STAGE_BYTES + 256 + Cfg::PARAM_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -341,22 +449,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         int buf = 0;
         uint32_t bphase = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&tfull[buf], bphase);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (!ok) { if (lane == 0) *abort_flag = 1; break; }
-            tc_fence_after();
             const int m0 = (tile / n_tiles) * kBlockM;
             const int n0 = (tile % n_tiles) * BN;
             const int m = m0 + row;
+            if constexpr (FLAVOR != 0) {
+                // Barrier A: every epilogue warp is done with the previous
+                // tile. The abort flag is only written after barrier B, so all
+                // warps read the same value here and leave the loop together.
+                epi_bar();
+                const bool stop = *abort_flag != 0;
+                if (!stop) stage_columns<BN, MODE, FLAVOR>(p, n0, N, colA, colB, gtab, ew * 32 + lane);
+                epi_bar();
+                if (stop) break;
+            }
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tfull[buf], bphase);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) {
+                if (lane == 0) *abort_flag = 1;
+                if constexpr (FLAVOR == 0) break;
+                else continue;  // keep meeting the named barriers until all warps see the flag
+            }
+            tc_fence_after();
+            if constexpr (FLAVOR == 0) {
 #pragma unroll 1
-            for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-                const int nc = n0 + c * 32;
-                if (nc >= N) break;  // warp-uniform
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + c * 32), acc);
-                tmem_ld_wait();
-                epi_chunk<MODE>(p, m, nc, acc, M, N);
+                for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                    const int nc = n0 + c * 32;
+                    if (nc >= N) break;  // warp-uniform
+                    uint32_t acc[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + c * 32), acc);
+                    tmem_ld_wait();
+                    epi_chunk<MODE>(p, m, nc, acc, M, N);
+                }
+            } else {
+                const bool live = m < M;
+                const int32_t rs = (p.wz && live) ? __ldg(p.rowsum + m) : 0;
+                int8_t *row8 = nullptr;
+                if constexpr (MODE == EPI_L8) {
+                    if (p.hm_T) {
+                        const int b = m / p.hm_T, t = m - (m / p.hm_T) * p.hm_T;
+                        row8 = reinterpret_cast<int8_t *>(p.out) + ((int64_t)b * p.hm_T + t) * 64;
+                    } else {
+                        row8 = reinterpret_cast<int8_t *>(p.out) + (int64_t)m * p.ldo;
+                    }
+                }
+                int32_t osum = 0;
+#pragma unroll 1
+                for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                    const int nc = n0 + c * 32;
+                    if (nc >= N) break;  // warp-uniform
+                    uint32_t acc[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + c * 32), acc);
+                    tmem_ld_wait();
+                    if (live) {
+                        int8_t *o8 = nullptr;
+                        if constexpr (MODE == EPI_L8)
+                            o8 = p.hm_T ? row8 + (int64_t)(nc >> 6) * p.hm_B * p.hm_T * 64 + (nc & 63) : row8 + nc;
+                        osum += epi_fast_chunk<MODE, FLAVOR>(p, m, nc, c * 32, rs, acc, colA, colB, gtab, o8);
+                    }
+                }
+                if (MODE == EPI_L8 && p.rowsum_out && live) atomicAdd(p.rowsum_out + m, osum);
             }
             tc_fence_before();
             __syncwarp();
@@ -385,9 +537,9 @@ int num_sms() {
     return n;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int FLAVOR>
 static cudaError_t launch_t(const GemmShape &g, const EpiParams &p, cudaStream_t stream) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, FLAVOR>;
     CUtensorMap ta, tb;
     cudaError_t e = make_tmap_2d_u8(&ta, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, kBlockM);
     if (e != cudaSuccess) return e;
@@ -395,21 +547,36 @@ static cudaError_t launch_t(const GemmShape &g, const EpiParams &p, cudaStream_t
     if (e != cudaSuccess) return e;
     static bool attr_set = false;
     if (!attr_set) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, MODE, FLAVOR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const int tiles = ((g.M + kBlockM - 1) / kBlockM) * ((g.N + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8_kernel<BN, MODE><<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, g.M, g.N, g.K, p);
+    gemm_i8_kernel<BN, MODE, FLAVOR><<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, g.M, g.N, g.K, p);
     return cudaGetLastError();
 }
 
-template <int MODE>
+template <int MODE, int FLAVOR>
 static cudaError_t launch_mode(const GemmShape &g, const EpiParams &p, cudaStream_t stream, int bn) {
-    if (bn == 64) return launch_t<64, MODE>(g, p, stream);
-    if (bn == 128) return launch_t<128, MODE>(g, p, stream);
-    return launch_t<256, MODE>(g, p, stream);
+    if (bn == 64) return launch_t<64, MODE, FLAVOR>(g, p, stream);
+    if (bn == 128) return launch_t<128, MODE, FLAVOR>(g, p, stream);
+    return launch_t<256, MODE, FLAVOR>(g, p, stream);
+}
+
+// The fast epilogue covers per-channel Linear8 (optionally with a GeLU
+// table, row sums and the head-major layout) and Linear32+Residual15 with
+// whole 32-column chunks and 16-byte aligned rows.
+static bool fast_eligible(const GemmShape &g, EpiMode mode, const EpiParams &p) {
+    if (!(mode == EPI_L8 || mode == EPI_L32_RES)) return false;
+    if (!p.per_channel || p.gelu || p.posadd || p.transpose_T || p.vt_T) return false;
+    if (g.N % 32) return false;
+    if (reinterpret_cast<uintptr_t>(p.out) & 15) return false;
+    if (mode == EPI_L8 && !p.hm_T && (p.ldo % 16)) return false;
+    if (mode == EPI_L32_RES && ((p.ldo % 8) || (p.ldr % 8) || (reinterpret_cast<uintptr_t>(p.res) & 15))) return false;
+    if (p.hm_T && (g.N % 64)) return false;
+    return true;
 }
 
 cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p, cudaStream_t stream, int bn_hint) {
@@ -425,13 +592,42 @@ cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p,
         if (m_tiles * ((g.N + 255) / 256) < num_sms() / 2) bn = 128;
         if (m_tiles * ((g.N + 127) / 128) < num_sms() / 2) bn = 64;
     }
+    if (p.gelu_tab && !fast_eligible(g, mode, p)) return cudaErrorInvalidValue;
+    if (fast_eligible(g, mode, p)) {
+        if (mode == EPI_L8) {
+            if (p.gelu_tab) return launch_mode<EPI_L8, 2>(g, p, stream, bn == 256 ? 128 : bn);
+            return launch_mode<EPI_L8, 1>(g, p, stream, bn);
+        }
+        return launch_mode<EPI_L32_RES, 1>(g, p, stream, bn);
+    }
     switch (mode) {
-    case EPI_ACC32: return launch_mode<EPI_ACC32>(g, p, stream, bn);
-    case EPI_L8: return launch_mode<EPI_L8>(g, p, stream, bn);
-    case EPI_L32: return launch_mode<EPI_L32>(g, p, stream, bn);
-    case EPI_L32_RES: return launch_mode<EPI_L32_RES>(g, p, stream, bn);
+    case EPI_ACC32: return launch_mode<EPI_ACC32, 0>(g, p, stream, bn);
+    case EPI_L8: return launch_mode<EPI_L8, 0>(g, p, stream, bn);
+    case EPI_L32: return launch_mode<EPI_L32, 0>(g, p, stream, bn);
+    case EPI_L32_RES: return launch_mode<EPI_L32_RES, 0>(g, p, stream, bn);
     }
     return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// GeLU lookup table: tab[n][x+128] = gelu_one(x) with channel n's parameters.
+// ---------------------------------------------------------------------------
+__global__ void gelu_table_kernel(const uint8_t *lut, const uint8_t *mi, const int8_t *si, const uint8_t *mo,
+                                  const int8_t *so, int n_in, int n_out, int N, int8_t *tab) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)N * 256) return;
+    const int n = (int)(i >> 8);
+    const int x = (int)(i & 255) - 128;
+    const int a = n_in == 1 ? 0 : n, b = n_out == 1 ? 0 : n;
+    tab[i] = (int8_t)gelu_one(x, lut, mi[a], (uint32_t)clampi(si[a], 0, 32), mo[b], (uint32_t)clampi(so[b], 0, 32));
+}
+
+cudaError_t gelu_table_build(const uint8_t *lut, const uint8_t *mi, const int8_t *si, const uint8_t *mo,
+                             const int8_t *so, int n_in, int n_out, int N, int8_t *tab, cudaStream_t st) {
+    const int64_t total = (int64_t)N * 256;
+    if (total <= 0) return cudaSuccess;
+    gelu_table_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(lut, mi, si, mo, so, n_in, n_out, N, tab);
+    return cudaGetLastError();
 }
 
 }  // namespace iw

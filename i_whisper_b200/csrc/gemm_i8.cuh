@@ -61,7 +61,15 @@ struct EpiParams {
     // optional: accumulate per-row sums of the int8 output (next GEMM's
     // zero-point term)
     int32_t *rowsum_out = nullptr;
+    // optional: per-channel GeLU as a lookup table [N][256] of int8 results
+    // indexed by (requantised value + 128); built by gelu_table_build from
+    // the same GeLU parameters, so it is exact
+    const int8_t *gelu_tab = nullptr;
 };
+
+// Builds tab[n][x+128] = GeLU_n(x) for x in [-128, 127] (gelu_scalar.cpp).
+cudaError_t gelu_table_build(const uint8_t *lut, const uint8_t *mi, const int8_t *si, const uint8_t *mo,
+                             const int8_t *so, int n_in, int n_out, int N, int8_t *tab, cudaStream_t st);
 
 struct GemmShape {
     const int8_t *x;

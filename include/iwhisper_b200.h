@@ -217,10 +217,21 @@ typedef struct iw_gemm_desc {
     int64_t headmajor_B;
     int32_t *out_rowsum;      /* [M]? accumulate row sums of the int8 output    */
     int tile_n;               /* 0 = automatic, else 64/128/256 */
+    /* per-channel GeLU as a lookup table [N][256] (from iw_gelu_table); use
+     * instead of the lut and luti/luto parameters on per-channel Linear8
+     * outputs */
+    const int8_t *gelu_table;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */
 int iw_gemm_i8(const iw_gemm_desc *d, void *stream);
+
+/* Per-channel GeLU lookup table for iw_gemm_desc.gelu_table:
+ * table[n][x+128] = GELU_int of x in [-128,127] with channel n's parameters
+ * (gelu_scalar.cpp:10-181; counts 1 or N as in iw_gelu). table is [N,256]. */
+int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,
+                  const uint8_t *luto_multiplier, const int8_t *luto_shift, int64_t luti_count, int64_t luto_count,
+                  int64_t N, int8_t *table, void *stream);
 
 typedef struct iw_attn_desc {
     /* element (b,t,h,d) of Q is q[b*q_bs + t*ldq + h*q_hs + d], same for

@@ -287,3 +287,56 @@ def test_device_status_clean():
     from i_whisper_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 4096), (129, 384, 1536), (7, 1280, 5120)])
+def test_linear8_gelu_table_rowsum(ops, L, M, K, N):
+    """fc1 form: Linear8 -> per-channel GeLU (lookup table) with the row sums
+    of the int8 output accumulated for the next GEMM's zero point."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(M + N)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=-2)
+    lut = rng.integers(0, 256, 16, dtype=np.uint8)
+    mi = rng.integers(0, 256, N, dtype=np.uint8); si = rng.integers(-2, 34, N).astype(np.int8)
+    mo = rng.integers(0, 256, N, dtype=np.uint8); so = rng.integers(-2, 34, N).astype(np.int8)
+    ref = L.gelu(L.linear8(x, w, b, wz, m, s), lut, mi, si, mo, so)
+    X, W = dev(x), dev(w)
+    tab = torch.empty(N, 256, dtype=torch.int8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    gp = [dev(a) for a in (lut, mi, si, mo, so)]
+    _lib.call("iw_gelu_table", *[t.data_ptr() for t in gp], N, N, N, tab.data_ptr(), st)
+    rs = torch.from_numpy(x.astype(np.int32).sum(1).astype(np.int32)).cuda()
+    out = torch.empty(M, N, dtype=torch.int8, device="cuda")
+    rs_out = torch.zeros(M, dtype=torch.int32, device="cuda")
+    B_, Z, Mu, S_ = dev(b), dev(wz), dev(m), dev(s)
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    d.mode, d.out, d.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
+    d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    d.gelu_table, d.out_rowsum = tab.data_ptr(), rs_out.data_ptr()
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
+    assert np.array_equal(host(out), ref)
+    assert np.array_equal(host(rs_out), ref.astype(np.int32).sum(1))
+
+
+@pytest.mark.parametrize("B,T,N", [(2, 1500, 768), (3, 37, 128)])
+def test_linear8_headmajor(ops, L, B, T, N):
+    """Cross-attention K/V form: Linear8 stored head-major [N/64, B, T, 64]."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(B * T)
+    K = 384
+    x, w, b, wz, m, s = rand_linear(rng, B * T, K, N)
+    ref = L.linear8(x, w, b, wz, m, s).reshape(B, T, N // 64, 64).transpose(2, 0, 1, 3)
+    X, W = dev(x), dev(w)
+    rs = torch.from_numpy(x.astype(np.int32).sum(1).astype(np.int32)).cuda()
+    out = torch.empty(N // 64, B, T, 64, dtype=torch.int8, device="cuda")
+    B_, Z, Mu, S_ = dev(b), dev(wz), dev(m), dev(s)
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = X.data_ptr(), K, W.data_ptr(), K, B * T, N, K
+    d.mode, d.out, d.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), 0
+    d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    d.headmajor_T, d.headmajor_B = T, B
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), torch.cuda.current_stream().cuda_stream))
+    assert np.array_equal(host(out), ref)
