@@ -54,6 +54,7 @@ SIGNATURES = {
     "iw_greedy_step": [_P, _I64, _P],
     "iw_add_i32": [_P, _I32, _P],
     "iw_gelu_table": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
+    "iw_shift_exp_table": [_I32, _P, _P],
 }
 
 IW_GEMM_ACC32, IW_GEMM_INT8, IW_GEMM_LINEAR32, IW_GEMM_LINEAR32_RES = 0, 1, 2, 3
@@ -86,6 +87,7 @@ class AttnDesc(C.Structure):
         ("Tk_dev", _P), ("Tk_cap", _I64), ("mask_mode", C.c_int), ("mask", _P),
         ("qk_multiplier", _U8), ("qk_shift", _I8), ("frac_bits", _I32),
         ("av_multiplier", _U8), ("av_shift", _I8), ("rsqrt_offset", _I32),
+        ("exp_table", _P), ("vt", _P), ("vt_ld", _I64),
     ]
 
 

@@ -450,7 +450,29 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream) {
     a.mask_mode = d->mask_mode; a.mask = d->mask;
     a.qk_mult = d->qk_multiplier; a.qk_shift = d->qk_shift; a.frac_bits = d->frac_bits;
     a.av_mult = d->av_multiplier; a.av_shift = d->av_shift; a.rsqrt_offset = (uint32_t)d->rsqrt_offset;
+    const bool tc = d->exp_table && d->vt && d->mask_mode == 0 && d->Tq == d->Tk && d->Tk > 0 && !d->Tk_dev &&
+                    d->q_hs == 64 && d->k_hs == 64 && d->v_hs == 64 && d->y_hs == 64 &&
+                    d->q_bs == d->Tq * d->ldq && d->k_bs == d->Tk * d->ldk && d->v_bs == d->Tk * d->ldv &&
+                    d->y_bs == d->Tq * d->ldy && (d->ldy % 16) == 0 && (reinterpret_cast<uintptr_t>(d->y) & 15) == 0 &&
+                    d->vt_ld >= d->Tk && (d->vt_ld % 16) == 0 && (reinterpret_cast<uintptr_t>(d->vt) & 15) == 0;
+    if (tc)
+        return cuda_check(iw::attention_tc(a, (int)d->B, (int)d->H, d->exp_table, d->vt, (int)d->vt_ld, S(stream)),
+                          "iw_attention_ex");
     return cuda_check(iw::attention_cc(a, (int)d->B, (int)d->H, S(stream)), "iw_attention_ex");
+}
+
+int iw_shift_exp_table(int32_t frac_bits, uint8_t *table, void *stream) {
+    if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    cudaStream_t st = S(stream);
+    Scratch sc(st);
+    if (int r = cuda_check(sc.alloc(2 * sizeof(int)), "iw_shift_exp_table")) return r;
+    if (int r = cuda_check(iw::shift_exp_table_build(frac_bits, table, (int *)sc.p, st), "iw_shift_exp_table")) return r;
+    int h[2] = {0, 0};
+    if (int r = cuda_check(cudaMemcpyAsync(h, sc.p, sizeof(h), cudaMemcpyDeviceToHost, st), "iw_shift_exp_table"))
+        return r;
+    if (int r = cuda_check(cudaStreamSynchronize(st), "iw_shift_exp_table")) return r;
+    if (h[1]) return fail(IW_EVALUE, "shift-exp table for frac_bits %d exceeds the tensor-core kernel", frac_bits);
+    return IW_OK;
 }
 
 int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,

@@ -10,7 +10,7 @@
 //                 k-step and commits to `empty[s]` (stage free) and to
 //                 `tfull[b]` (accumulator ready).
 //   warps 2..9  : epilogue. Warp w reads TMEM lanes 32*(w%4)..+31 (its
-//                 lane quadrant) and half of the BN columns, applies the
+//                 lane quadrant) and every 4th 32-column chunk, applies the
 //                 requantisation of the layer (bias, zero point, MULH,
 //                 rounding shift, clamp, optional GeLU / Residual15 /
 //                 positional add) and stores straight to global memory,
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int ew = warp - 2;
         const int quad = warp & 3;
-        const int half = ew >> 2;
+        const int slice = ew >> 2;  // which of the kEpiWarps/4 column slices this warp takes
         const int row = quad * 32 + lane;
         int buf = 0;
         uint32_t bphase = 0;
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             if constexpr (FLAVOR == 0) {
 #pragma unroll 1
-                for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                for (int c = slice; c < BN / 32; c += kEpiWarps / 4) {
                     const int nc = n0 + c * 32;
                     if (nc >= N) break;  // warp-uniform
                     uint32_t acc[32];
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 int32_t osum = 0;
 #pragma unroll 1
-                for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                for (int c = slice; c < BN / 32; c += kEpiWarps / 4) {
                     const int nc = n0 + c * 32;
                     if (nc >= N) break;  // warp-uniform
                     uint32_t acc[32];

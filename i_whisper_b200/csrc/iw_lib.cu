@@ -3,4 +3,5 @@
 // definition and cross-file device functions inline without -rdc.
 #include "gemm_i8.cu"
 #include "kernels.cu"
+#include "attn_tc.cu"
 #include "capi.cu"

@@ -65,6 +65,16 @@ cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K,
 cudaError_t pad_rows(const int8_t *x, int64_t rows, int64_t cols, int8_t *out, int64_t ldo, cudaStream_t st);
 cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st);
 
+// Tensor-core attention for unmasked self-attention with Tq == Tk (encoder):
+// Q/K rows straight from the projection buffer (16-byte aligned, batch
+// stride T*ld, head h at column h*64), V transposed into vt [B*H*64, vt_ld]
+// (vt_ld >= T, multiple of 16). tab from shift_exp_table_build.
+cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld, cudaStream_t st);
+// Builds the shift-exp table for frac_bits fb into tab (>= 32772 bytes);
+// scratch2 is two device ints, scratch2[1] == 1 afterwards when the table is
+// too long for the tensor-core kernel.
+cudaError_t shift_exp_table_build(int32_t fb, uint8_t *tab, int *scratch2, cudaStream_t st);
+
 // Append one position of self-attention K and V (row b of src, columns
 // [k_col, k_col+H*64) and [v_col, v_col+H*64)) to head-major caches
 // [B, H, Tcap, 64] at position *pos_dev (or `pos` when pos_dev is null).

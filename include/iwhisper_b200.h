@@ -247,9 +247,22 @@ typedef struct iw_attn_desc {
     const uint8_t *mask;
     uint8_t qk_multiplier; int8_t qk_shift; int32_t frac_bits;
     uint8_t av_multiplier; int8_t av_shift; int32_t rsqrt_offset;
+    /* tensor-core path for unmasked self-attention with Tq == Tk and
+     * contiguous batches: the shift-exp table of iw_shift_exp_table for this
+     * frac_bits, and a V^T buffer [B*H*64, vt_ld] (vt_ld >= Tk, multiple of
+     * 16) the call fills. NULL selects the CUDA-core kernel. */
+    const uint8_t *exp_table;
+    int8_t *vt;
+    int64_t vt_ld;
 } iw_attn_desc;
 
 int iw_attention_ex(const iw_attn_desc *d, void *stream);
+
+/* Shift-exp table (attention_scalar.cpp:388-560 as a function of the int16
+ * difference to rowmax+1) for the tensor-core attention; table needs 32772
+ * bytes. Synchronises `stream`; IW_EVALUE when frac_bits makes the table too
+ * long for the tensor-core kernel (use the CUDA-core path then). */
+int iw_shift_exp_table(int32_t frac_bits, uint8_t *table, void *stream);
 
 /* LayerNorm32 over rows with strides; optionally writes the row sums of the
  * int8 output (rowsum_out) and zeroes rowsum_zero[rows] for a later

@@ -340,3 +340,40 @@ def test_linear8_headmajor(ops, L, B, T, N):
     d.headmajor_T, d.headmajor_B = T, B
     _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), torch.cuda.current_stream().cuda_stream))
     assert np.array_equal(host(out), ref)
+
+
+@pytest.mark.parametrize("B,H,T", [(2, 6, 1500), (1, 16, 1500), (2, 8, 130), (3, 4, 64), (1, 6, 257)])
+@pytest.mark.parametrize("qk_s,fb", [(10, 7), (12, 7), (0, 7), (14, 9), (8, 5)])
+def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
+    """Encoder self-attention on the tcgen05 path (exp table + V^T) against
+    the oracle's three reference stages."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(B * 1000 + H * 10 + T + qk_s)
+    d = H * 64
+    qkv = rng.integers(-127, 128, (B * T, 3 * d), dtype=np.int8)
+    q = qkv[:, :d].reshape(B, T, d); k = qkv[:, d:2 * d].reshape(B, T, d); v = qkv[:, 2 * d:].reshape(B, T, d)
+    P = {"a.qk_req_multiplier": np.array([90], np.uint8), "a.qk_req_shiftmount": np.array([qk_s], np.int8),
+         "a.qk_frac_bits": np.array(fb, np.int32), "a.av_req_multiplier": np.array([200], np.uint8),
+         "a.av_req_shiftmount": np.array([8], np.int8)}
+    ref = O.attention_core(L, P, "a", q, k, v, H, None)
+    st = torch.cuda.current_stream().cuda_stream
+    tab = torch.empty(32772, dtype=torch.uint8, device="cuda")
+    _lib.call("iw_shift_exp_table", fb, tab.data_ptr(), st)
+    QKV = dev(qkv)
+    vt_ld = (T + 15) // 16 * 16
+    vt = torch.empty(B * H * 64, vt_ld, dtype=torch.int8, device="cuda")
+    out = torch.empty(B * T, d, dtype=torch.int8, device="cuda")
+    a = _lib.AttnDesc()
+    base = QKV.data_ptr()
+    a.q, a.ldq, a.q_bs, a.q_hs = base, 3 * d, T * 3 * d, 64
+    a.k, a.ldk, a.k_bs, a.k_hs = base + d, 3 * d, T * 3 * d, 64
+    a.v, a.ldv, a.v_bs, a.v_hs = base + 2 * d, 3 * d, T * 3 * d, 64
+    a.y, a.ldy, a.y_bs, a.y_hs = out.data_ptr(), d, T * d, 64
+    a.B, a.H, a.Tq, a.Tk = B, H, T, T
+    a.qk_multiplier, a.qk_shift, a.frac_bits = 90, qk_s, fb
+    a.av_multiplier, a.av_shift, a.rsqrt_offset = 200, 8, 16
+    a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
+    _lib.check(_lib.LIB.iw_attention_ex(ctypes.byref(a), st))
+    assert np.array_equal(host(out).reshape(B, T, d), ref)
+    assert _lib.device_status(clear=True) == 0
