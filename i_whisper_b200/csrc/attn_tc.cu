@@ -36,11 +36,12 @@ namespace iw {
 
 namespace attn {
 
-constexpr int BQ = 128;     // query rows per CTA
+constexpr int BQ = 128;     // query rows per work item
 constexpr int BK = 128;     // keys per block
 constexpr int KST = 4;      // K stages
 constexpr int VST = 3;      // V^T stages
-constexpr int SOFT_WARPS = 8;
+constexpr int SBUF = 3;     // S accumulators in TMEM
+constexpr int SOFT_WARPS = 16;  // four per TMEM lane quadrant, 32 keys each
 constexpr int THREADS = 64 + 32 * SOFT_WARPS;
 constexpr int TAB_MAX = 4096;  // entries of the shift-exp table kept in shared memory
 
@@ -49,15 +50,17 @@ constexpr int K_BYTES = BK * 64;
 constexpr int V_BYTES = 64 * BK;
 constexpr int P_BYTES = BQ * BK;
 // layout (offsets from the 1024-aligned base)
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_Q = 0;                          // two Q buffers
+constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
-constexpr int OFF_P = OFF_V + VST * V_BYTES;
+constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
 constexpr int OFF_TAB = OFF_P + 2 * P_BYTES;
-constexpr int OFF_RED = OFF_TAB + TAB_MAX;  // [2][BQ] int32 cross-warp row reductions
-constexpr int OFF_BAR = OFF_RED + 2 * BQ * 4;
-constexpr int SMEM = 1024 + OFF_BAR + 256;
-constexpr uint32_t TMEM_COLS = 256;  // S at columns [0,128), O at [128,192); two CTAs per SM
+constexpr int OFF_RED = OFF_TAB + TAB_MAX;        // [4][BQ] int32 cross-warp row reductions
+constexpr int OFF_BAR = OFF_RED + 4 * BQ * 4;
+constexpr int SMEM = 1024 + OFF_BAR + 512;
+constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
+constexpr uint32_t TMEM_O = 384;
+static_assert(OFF_V % 1024 == 0 && OFF_P % 1024 == 0, "swizzle-128 tiles need 1024-byte alignment");
 }  // namespace attn
 
 struct AttnTcParams {
@@ -86,12 +89,23 @@ IW_DEV uint64_t sdesc_kmajor_sw64(uint32_t saddr) {
 
 IW_DEV void bar_soft() { asm volatile("bar.sync 1, %0;" ::"n"(attn::SOFT_WARPS * 32) : "memory"); }
 
+// Score requantisation for 1 <= m <= 255 and shift in [1,31]:
+// rrs(acc*m, s) = (acc*m + 2^(s-1) - signbit(acc*m)) >> s, and since
+// |acc*m| < 2^31 and m > 0, signbit(acc*m) == signbit(acc) == -mulhi(acc, 1).
+IW_DEV int32_t score_fast(uint32_t acc, uint32_t m, uint32_t rnd, uint32_t sh) {
+    int32_t x, y;
+    asm("mad.lo.s32 %0, %1, %2, %3;" : "=r"(x) : "r"(acc), "r"(m), "r"(rnd));
+    asm("mad.hi.s32 %0, %1, 1, %2;" : "=r"(y) : "r"(acc), "r"(x));
+    return y >> sh;
+}
+
 IW_DEV int32_t rrs_masked(int32_t x, const AttnTcParams &p) {
     const uint32_t t = (uint32_t)x + p.qk_rnd + ((uint32_t)(x >> 31) & p.qk_sgn);
     return (int32_t)(((int32_t)t >> p.qk_sh) & (int32_t)p.qk_z);
 }
 
-__global__ void __launch_bounds__(attn::THREADS, 2)
+template <bool FAST>
+__global__ void __launch_bounds__(attn::THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
     using namespace attn;
@@ -104,40 +118,40 @@ __global__ void __launch_bounds__(attn::THREADS, 2)
     uint8_t *sTab = smem + OFF_TAB;
     int32_t *sRed = reinterpret_cast<int32_t *>(smem + OFF_RED);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *q_full = bars;
-    uint64_t *k_full = bars + 1;             // [KST]
+    uint64_t *q_full = bars;                 // [2]
+    uint64_t *q_empty = q_full + 2;          // [2]
+    uint64_t *k_full = q_empty + 2;          // [KST]
     uint64_t *k_empty = k_full + KST;        // [KST]
     uint64_t *v_full = k_empty + KST;        // [VST]
     uint64_t *v_empty = v_full + VST;        // [VST]
-    uint64_t *s_full = v_empty + VST;        // [1]
-    uint64_t *s_empty = s_full + 1;          // [1]
-    uint64_t *p_full = s_empty + 1;          // [2]
+    uint64_t *s_full = v_empty + VST;        // [SBUF]
+    uint64_t *s_empty = s_full + SBUF;       // [SBUF]
+    uint64_t *p_full = s_empty + SBUF;       // [2]
     uint64_t *p_empty = p_full + 2;          // [2]
-    uint64_t *o_full = p_empty + 2;
-    uint64_t *drain = o_full + 1;
+    uint64_t *o_full = p_empty + 2;          // [2]
+    uint64_t *o_empty = o_full + 2;          // [2]
+    uint64_t *drain = o_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile uint32_t *abort_flag = tmem_slot + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = p.T, H = p.H;
     const int nqb = (T + BQ - 1) / BQ;
-    const int qb = blockIdx.x % nqb;
-    const int bh = blockIdx.x / nqb;
-    const int h = bh % H, b = bh / H;
-    const int q0 = qb * BQ;
     const int nkb = (T + BK - 1) / BK;
+    const int items = p.B * H * nqb;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (int s = 0; s < KST; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
-        for (int s = 0; s < VST; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
-        mbar_init(s_full, 1);
-        mbar_init(s_empty, SOFT_WARPS);
         for (int s = 0; s < 2; ++s) {
+            mbar_init(&q_full[s], 1);
+            mbar_init(&q_empty[s], 1);
             mbar_init(&p_full[s], SOFT_WARPS);
             mbar_init(&p_empty[s], 1);
+            mbar_init(&o_full[s], 1);
+            mbar_init(&o_empty[s], SOFT_WARPS);
         }
-        mbar_init(o_full, 1);
+        for (int s = 0; s < KST; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
+        for (int s = 0; s < VST; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
+        for (int s = 0; s < SBUF; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], SOFT_WARPS); }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -152,119 +166,145 @@ __global__ void __launch_bounds__(attn::THREADS, 2)
     const uint32_t tmem_base = *tmem_slot;
 
     // Q and K maps cover [B*T rows, H*64 columns]; V^T maps [B*H*64, vt_ld].
-    const int row0 = b * T;
-
     if (warp == 0) {
         if (lane == 0) {
-            // Q once
-            mbar_arrive_expect_tx(q_full, Q_BYTES);
-            tma_load_2d(&tmQ, q_full, sQ, h * 64, row0 + q0);
-            int ks = 0;
-            uint32_t kph = 0;
-            int vs = 0;
-            uint32_t vph = 0;
+            int qs = 0, ks = 0, vs = 0;
+            uint32_t qph = 0, kph = 0, vph = 0;
             bool ok = true;
-            for (int pass = 0; pass < 2 && ok; ++pass) {
-                for (int j = 0; j < nkb && ok; ++j) {
-                    if (!mbar_wait(&k_empty[ks], kph ^ 1)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&k_full[ks], K_BYTES);
-                    tma_load_2d(&tmK, &k_full[ks], sK + ks * K_BYTES, h * 64, row0 + j * BK);
-                    if (++ks == KST) { ks = 0; kph ^= 1; }
-                    if (pass == 1) {
-                        if (!mbar_wait(&v_empty[vs], vph ^ 1)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
-                        tma_load_2d(&tmV, &v_full[vs], sV + vs * V_BYTES, j * BK, bh * 64);
-                        if (++vs == VST) { vs = 0; vph ^= 1; }
+            for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
+                const int qb = it % nqb, bh = it / nqb;
+                const int h = bh % H, row0 = (bh / H) * T;
+                if (!mbar_wait(&q_empty[qs], qph ^ 1)) { ok = false; break; }
+                mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
+                tma_load_2d(&tmQ, &q_full[qs], sQ + qs * Q_BYTES, h * 64, row0 + qb * BQ);
+                if (++qs == 2) { qs = 0; qph ^= 1; }
+                for (int pass = 0; pass < 2 && ok; ++pass) {
+                    for (int j = 0; j < nkb; ++j) {
+                        if (!mbar_wait(&k_empty[ks], kph ^ 1)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&k_full[ks], K_BYTES);
+                        tma_load_2d(&tmK, &k_full[ks], sK + ks * K_BYTES, h * 64, row0 + j * BK);
+                        if (++ks == KST) { ks = 0; kph ^= 1; }
+                        if (pass == 1) {
+                            if (!mbar_wait(&v_empty[vs], vph ^ 1)) { ok = false; break; }
+                            mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
+                            tma_load_2d(&tmV, &v_full[vs], sV + vs * V_BYTES, j * BK, bh * 64);
+                            if (++vs == VST) { vs = 0; vph ^= 1; }
+                        }
                     }
                 }
             }
             if (!ok) *abort_flag = 1;
-            // all issued copies must land before exit (bounded)
-            mbar_wait(q_full, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_i8(BQ, BK, true, true);
             constexpr uint32_t idesc_pv = idesc_i8(BQ, 64, false, true);
-            const uint32_t tS = tmem_base, tO = tmem_base + 128;
-            int ks = 0, sb = 0, pb = 0, vs = 0;
-            uint32_t kph = 0, sph = 0, pph = 0, vph = 0;
-            bool ok = mbar_wait(q_full, 0);
-            tc_fence_after();
-            const uint32_t qa = smem_u32(sQ);
-            auto issue_qk = [&](int j) -> bool {
-                if (!mbar_wait(&s_empty[sb], sph ^ 1)) return false;
-                if (!mbar_wait(&k_full[ks], kph)) return false;
+            int qs = 0, ks = 0, sb = 0, pb = 0, vs = 0, ob = 0;
+            uint32_t qph = 0, kph = 0, sph = 0, pph = 0, vph = 0, oph = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
+                if (!mbar_wait(&q_full[qs], qph)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t ka = smem_u32(sK + ks * K_BYTES);
-                const uint32_t d = tS + (uint32_t)(sb * BK);
+                const uint32_t qa = smem_u32(sQ + qs * Q_BYTES);
+                auto issue_qk = [&]() -> bool {
+                    if (!mbar_wait(&s_empty[sb], sph ^ 1)) return false;
+                    if (!mbar_wait(&k_full[ks], kph)) return false;
+                    tc_fence_after();
+                    const uint32_t ka = smem_u32(sK + ks * K_BYTES);
+                    const uint32_t d = tmem_base + (uint32_t)(sb * BK);
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk)
-                    mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
-                mma_commit(&k_empty[ks]);
-                mma_commit(&s_full[sb]);
-                if (++ks == KST) { ks = 0; kph ^= 1; }
-                sph ^= 1;
-                return true;
-            };
-            // pass 1
-            for (int j = 0; j < nkb && ok; ++j) ok = issue_qk(j);
-            // pass 2: QK of block j+1 is issued before PV of block j
-            if (ok) ok = issue_qk(0);
-            for (int j = 0; j < nkb && ok; ++j) {
-                if (j + 1 < nkb) ok = issue_qk(j + 1);
+                    for (int kk = 0; kk < 2; ++kk)
+                        mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
+                    mma_commit(&k_empty[ks]);
+                    mma_commit(&s_full[sb]);
+                    if (++ks == KST) { ks = 0; kph ^= 1; }
+                    if (++sb == SBUF) { sb = 0; sph ^= 1; }
+                    return true;
+                };
+                // pass 1
+                for (int j = 0; j < nkb && ok; ++j) ok = issue_qk();
+                // pass 2: QK of block j+1 is issued before P.V of block j
+                if (ok) ok = issue_qk();
+                for (int j = 0; j < nkb && ok; ++j) {
+                    if (j + 1 < nkb) ok = issue_qk();
+                    if (!ok) break;
+                    if (j + 1 == nkb) mma_commit(&q_empty[qs]);  // every QK of this item issued
+                    if (!mbar_wait(&p_full[pb], pph) || !mbar_wait(&v_full[vs], vph)) { ok = false; break; }
+                    if (j == 0 && !mbar_wait(&o_empty[ob], oph ^ 1)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t pa = smem_u32(sP + pb * P_BYTES);
+                    const uint32_t va = smem_u32(sV + vs * V_BYTES);
+                    const uint32_t tO = tmem_base + TMEM_O + (uint32_t)(ob * 64);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; ++kk)
+                        mma_i8(tO, sdesc_kmajor_sw128(pa + kk * 32), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
+                               (j | kk) != 0);
+                    mma_commit(&v_empty[vs]);
+                    mma_commit(&p_empty[pb]);
+                    if (++vs == VST) { vs = 0; vph ^= 1; }
+                    if (++pb == 2) { pb = 0; pph ^= 1; }
+                }
                 if (!ok) break;
-                if (!mbar_wait(&p_full[pb], pph)) { ok = false; break; }
-                if (!mbar_wait(&v_full[vs], vph)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t pa = smem_u32(sP + pb * P_BYTES);
-                const uint32_t va = smem_u32(sV + vs * V_BYTES);
-#pragma unroll
-                for (int kk = 0; kk < BK / 32; ++kk)
-                    mma_i8(tO, sdesc_kmajor_sw128(pa + kk * 32), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
-                           (j | kk) != 0);
-                mma_commit(&v_empty[vs]);
-                mma_commit(&p_empty[pb]);
-                if (++vs == VST) { vs = 0; vph ^= 1; }
-                if (++pb == 2) { pb = 0; pph ^= 1; }
+                mma_commit(&o_full[ob]);
+                if (++ob == 2) { ob = 0; oph ^= 1; }
+                if (++qs == 2) { qs = 0; qph ^= 1; }
             }
-            if (ok) mma_commit(o_full);
-            else *abort_flag = 1;
+            if (!ok) *abort_flag = 1;
             mma_commit(drain);
             mbar_wait(drain, 0);
         }
     } else {
         // ------------------------------------------------------------------
-        // softmax warps
+        // softmax warps: thread = query row of the warp's TMEM lane quadrant,
+        // the warp's slice = 32 of the 128 key columns of every block
         // ------------------------------------------------------------------
         const int sw = warp - 2;
         const int quad = warp & 3;
-        const int half = sw >> 2;  // 0: key columns [0,64), 1: [64,128) of each block
-        const int r = quad * 32 + lane;  // query row within the block
+        const int slice = sw >> 2;
+        const int r = quad * 32 + lane;  // query row within the work item
         const int et = sw * 32 + lane;
-        // shift-exp table
         // index of the zero entry (bounded by the shared-memory table size)
         const uint32_t t1 = min((uint32_t)p.tab[0] | ((uint32_t)p.tab[1] << 8), (uint32_t)(TAB_MAX - 1));
         for (uint32_t i = et; i <= t1; i += SOFT_WARPS * 32) sTab[i] = p.tab[2 + i];
-        bar_soft();
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        // ---- pass 1: raw row max ------------------------------------------
-        int32_t mx = INT32_MIN;
-        int sb = 0;
-        uint32_t sph = 0;
+        const uint32_t col = (uint32_t)(slice * 32);
+        int sb = 0, pb = 0, ob = 0;
+        uint32_t sph = 0, pph = 0, oph = 0;
+        // wait helper: lane 0 waits, the warp agrees; once a wait failed the
+        // warp stops waiting (and computing) but keeps meeting the barriers
         bool ok = true;
-        for (int j = 0; j < nkb; ++j) {
-            bool w = true;
-            if (lane == 0) w = mbar_wait(&s_full[sb], sph);
-            if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) { ok = false; break; }
-            tc_fence_after();
-            const int kbase = j * BK + half * 64;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
+        auto wait_all = [&](uint64_t *bar, uint32_t parity) {
+            bool w = ok;
+            if (ok && lane == 0) w = mbar_wait(bar, parity);
+            w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+            if (!w && ok) {
+                ok = false;
+                if (lane == 0) *abort_flag = 1;
+            }
+            return ok;
+        };
+        for (int it = blockIdx.x; it < items; it += gridDim.x) {
+            // every softmax warp reads the abort flag between the same two
+            // barriers (it is only written outside them) and leaves together
+            bar_soft();
+            const bool stop = *abort_flag != 0;
+            bar_soft();
+            if (stop) break;
+            const int qb = it % nqb, bh = it / nqb;
+            const int h = bh % H, row0 = (bh / H) * T;
+            const int q0 = qb * BQ;
+            // ---- pass 1: raw row max ------------------------------------------
+            int32_t mx = INT32_MIN;
+            for (int j = 0; j < nkb; ++j) {
+                if (!wait_all(&s_full[sb], sph)) break;
+                tc_fence_after();
                 uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK + half * 64 + c * 32), acc);
+                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK) + col, acc);
                 tmem_ld_wait();
-                const int valid = T - (kbase + c * 32);  // keys of this chunk that exist
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[sb]);  // S is in registers: release it early
+                const int valid = T - (j * BK + slice * 32);
                 if (valid >= 32) {
 #pragma unroll
                     for (int u = 0; u < 32; ++u) mx = max(mx, (int32_t)acc[u]);
@@ -273,99 +313,109 @@ __global__ void __launch_bounds__(attn::THREADS, 2)
                     for (int u = 0; u < 32; ++u)
                         if (u < valid) mx = max(mx, (int32_t)acc[u]);
                 }
+                if (++sb == SBUF) { sb = 0; sph ^= 1; }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[sb]);
-            sph ^= 1;
-        }
-        // combine the two column halves of each row
-        if (half == 1) sRed[r] = mx;
-        bar_soft();
-        if (half == 0) sRed[r] = max(mx, sRed[r]);
-        bar_soft();
-        mx = sRed[r];
-        // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
-        int32_t smax = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
-        smax = clampi(smax, -32768, 32767);
-        const int32_t rmax1 = (int32_t)(int16_t)(smax + 1);
-        // ---- pass 2: exp, row sum, P to shared memory ----------------------
-        int32_t rsum = 0;
-        int pb = 0;
-        uint32_t pph = 0;
-        for (int j = 0; j < nkb && ok; ++j) {
-            bool w = true;
-            if (lane == 0) w = mbar_wait(&s_full[sb], sph) && mbar_wait(&p_empty[pb], pph ^ 1);
-            if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) { ok = false; break; }
-            tc_fence_after();
-            const int kbase = j * BK + half * 64;
-            uint8_t *prow = sP + pb * P_BYTES + r * 128;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            // combine the four column slices of each row
+            sRed[slice * BQ + r] = mx;
+            bar_soft();
+            mx = max(max(sRed[r], sRed[BQ + r]), max(sRed[2 * BQ + r], sRed[3 * BQ + r]));
+            bar_soft();
+            // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
+            int32_t smax = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
+            smax = clampi(smax, -32768, 32767);
+            const int32_t rmax1 = (int32_t)(int16_t)(smax + 1);
+            // For a row whose requantised max is below 32767 (no int16 wrap of
+            // rowmax+1) and whose rowmax1 + 32768 >= t1, neither the int16 clamp
+            // of a score nor the int16 wrap of its difference can change the
+            // table index: idx = min(rowmax1 - s, t1) with s unclamped. The warp
+            // uses that path only when all of its 32 rows qualify.
+            const bool warp_simple = __all_sync(0xffffffffu, rmax1 != -32768 && rmax1 + 32768 >= (int32_t)t1);
+            // ---- pass 2: exp, row sum, P to shared memory ----------------------
+            int32_t rsum = 0;
+            for (int j = 0; j < nkb; ++j) {
+                if (!wait_all(&s_full[sb], sph)) break;
+                tc_fence_after();
                 uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK + half * 64 + c * 32), acc);
+                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK) + col, acc);
                 tmem_ld_wait();
-                const int valid = T - (kbase + c * 32);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[sb]);
+                const int valid = T - (j * BK + slice * 32);
                 uint32_t w4[8];
+                if (FAST && warp_simple && valid >= 32) {
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    int32_t s = rrs_masked((int32_t)(acc[u] * p.qk_mult), p);
-                    s = clampi(s, -32768, 32767);
-                    const int32_t xs = (int32_t)(int16_t)(s - rmax1);
-                    const uint32_t idx = min((uint32_t)(-xs), t1);
-                    uint32_t e = sTab[idx];
-                    if (valid < 32 && u >= valid) e = 0;
-                    rsum += (int32_t)e;
-                    if ((u & 3) == 0) w4[u >> 2] = 0;
-                    w4[u >> 2] |= e << (8 * (u & 3));
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        uint32_t ww = 0;
+#pragma unroll
+                        for (int k4 = 0; k4 < 4; ++k4) {
+                            const int32_t sc = score_fast(acc[q4 * 4 + k4], p.qk_mult, p.qk_rnd, p.qk_sh);
+                            const uint32_t idx = min((uint32_t)(rmax1 - sc), t1);
+                            ww += (uint32_t)sTab[idx] << (8 * k4);
+                        }
+                        rsum = __dp4a((int32_t)ww, 0x01010101, rsum);
+                        w4[q4] = ww;
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) {
+                        int32_t sc;
+                        if constexpr (FAST) sc = score_fast(acc[u], p.qk_mult, p.qk_rnd, p.qk_sh);
+                        else sc = rrs_masked((int32_t)(acc[u] * p.qk_mult), p);
+                        sc = clampi(sc, -32768, 32767);
+                        // int16 wrap of -(s - rowmax1), clamped to the zero entry
+                        const uint32_t idx = min((uint32_t)(rmax1 - sc) & 0xFFFFu, t1);
+                        const uint32_t e = u < valid ? (uint32_t)sTab[idx] : 0u;
+                        rsum += (int32_t)e;
+                        if ((u & 3) == 0) w4[u >> 2] = e;
+                        else w4[u >> 2] |= e << (8 * (u & 3));
+                    }
                 }
+                // the P buffer must be free (P.V of block j-2 done)
+                if (!wait_all(&p_empty[pb], pph ^ 1)) break;
                 // two 16-byte chunks of this row; 128-byte swizzle: chunk k of
                 // row r lives at chunk (k ^ (r & 7))
-                const int ch0 = half * 4 + c * 2;
+                uint8_t *prow = sP + pb * P_BYTES + r * 128;
+                const int ch0 = slice * 2;
                 *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                 *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(w4[4], w4[5], w4[6], w4[7]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[pb]);
+                if (++sb == SBUF) { sb = 0; sph ^= 1; }
+                if (++pb == 2) { pb = 0; pph ^= 1; }
             }
-            tc_fence_before();
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&s_empty[sb]);
-                mbar_arrive(&p_full[pb]);
-            }
-            sph ^= 1;
-            if (++pb == 2) { pb = 0; pph ^= 1; }
-        }
-        // combine row sums
-        if (half == 1) sRed[BQ + r] = rsum;
-        bar_soft();
-        if (half == 0) sRed[BQ + r] += rsum;
-        bar_soft();
-        rsum = sRed[BQ + r];
-        // ---- epilogue: O / normalise / AV requant ---------------------------
-        bool w = ok;
-        if (ok && lane == 0) w = mbar_wait(o_full, 0);
-        if (__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
-            tc_fence_after();
-            uint32_t acc[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_base + 128u + (uint32_t)(half * 32), acc);
-            tmem_ld_wait();
-            const int q = q0 + r;
-            if (q < T) {
-                const int32_t inv = fisr(rsum, p.rsqrt_offset);
-                uint32_t w4[8];
+            // combine row sums
+            sRed[slice * BQ + r] = rsum;
+            bar_soft();
+            rsum = sRed[r] + sRed[BQ + r] + sRed[2 * BQ + r] + sRed[3 * BQ + r];
+            // ---- epilogue: O / normalise / AV requant ---------------------------
+            if (wait_all(&o_full[ob], oph)) {
+                tc_fence_after();
+                uint32_t acc[16];
+                tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * 16), acc);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[ob]);
+                const int q = q0 + r;
+                if (q < T) {
+                    const int32_t inv = fisr(rsum, p.rsqrt_offset);
+                    uint32_t w4[4];
 #pragma unroll
-                for (int u = 0; u < 32; ++u) {
-                    int32_t v = rrs(wmul((int32_t)acc[u], inv), p.rsqrt_offset);
-                    v = rrs(wmul(v, inv), p.rsqrt_offset);
-                    v = rrs(wmul(v, (int32_t)p.av_mult), p.av_shift);
-                    v = clampi(v, -127, 127);
-                    if ((u & 3) == 0) w4[u >> 2] = 0;
-                    w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                    for (int u = 0; u < 16; ++u) {
+                        int32_t v = rrs(wmul((int32_t)acc[u], inv), p.rsqrt_offset);
+                        v = rrs(wmul(v, inv), p.rsqrt_offset);
+                        v = rrs(wmul(v, (int32_t)p.av_mult), p.av_shift);
+                        v = clampi(v, -127, 127);
+                        if ((u & 3) == 0) w4[u >> 2] = 0;
+                        w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                    }
+                    int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * 16;
+                    *reinterpret_cast<uint4 *>(o) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                 }
-                int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + half * 32;
-                *reinterpret_cast<uint4 *>(o) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                *reinterpret_cast<uint4 *>(o + 16) = make_uint4(w4[4], w4[5], w4[6], w4[7]);
             }
+            if (++ob == 2) { ob = 0; oph ^= 1; }
         }
     }
     tc_fence_before();
@@ -455,12 +505,17 @@ cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, in
     p.vt_ld = vt_ld;
     static bool attr = false;
     if (!attr) {
-        e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    const int grid = B * H * ((T + BQ - 1) / BQ);
-    attn_tc_kernel<<<grid, THREADS, SMEM, st>>>(tq, tk, tv, p);
+    const int items = B * H * ((T + BQ - 1) / BQ);
+    const int grid = items < num_sms() ? items : num_sms();
+    const bool fast = a.qk_mult >= 1 && a.qk_mult <= 255 && sh >= 1 && sh <= 31;
+    if (fast) attn_tc_kernel<true><<<grid, THREADS, SMEM, st>>>(tq, tk, tv, p);
+    else attn_tc_kernel<false><<<grid, THREADS, SMEM, st>>>(tq, tk, tv, p);
     return cudaGetLastError();
 }
 
