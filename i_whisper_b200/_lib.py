@@ -55,9 +55,11 @@ SIGNATURES = {
     "iw_add_i32": [_P, _I32, _P],
     "iw_gelu_table": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
     "iw_shift_exp_table": [_I32, _P, _P],
+    "iw_linear8_noalloc": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
 }
 
 IW_GEMM_ACC32, IW_GEMM_INT8, IW_GEMM_LINEAR32, IW_GEMM_LINEAR32_RES = 0, 1, 2, 3
+NOALLOC_MAX_ROWS = 65536  # IW_NOALLOC_MAX_ROWS
 
 
 class GemmDesc(C.Structure):

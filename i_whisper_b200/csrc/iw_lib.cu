@@ -5,3 +5,4 @@
 #include "kernels.cu"
 #include "attn_tc.cu"
 #include "capi.cu"
+#include "noalloc.cu"

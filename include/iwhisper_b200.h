@@ -309,6 +309,30 @@ int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream);
 /* *p += v on the device (advances device-side decode counters). */
 int iw_add_i32(int32_t *p, int32_t v, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free Linear8. This entry point has no counterpart in the
+ * reference: it exists for callers that cannot allocate device memory while
+ * they run -- work captured into a CUDA graph whose memory pool they do not
+ * own, servers that plan all device memory up front and forbid allocator
+ * traffic on the request path, or hosts that only hand over raw pointers
+ * from another runtime. It computes exactly what iw_linear8 computes, but the
+ * row sums of x needed by the weight zero points live in one fixed device
+ * array of IW_NOALLOC_MAX_ROWS int32 (256 KiB) that every GPU loading this
+ * library keeps until the process exits, instead of a scratch allocation.
+ *   - M must not exceed IW_NOALLOC_MAX_ROWS; K must be a multiple of 16 and
+ *     x, weight 16-byte aligned (no padding copy is made); otherwise the call
+ *     returns IW_EINVAL with a message and launches nothing.
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents: calls
+ *     whose executions overlap on the GPU race, so order them on one stream.
+ *   - No cudaMalloc, cudaFree or other allocating routine is called.
+ * ---------------------------------------------------------------------- */
+#define IW_NOALLOC_MAX_ROWS 65536
+int iw_linear8_noalloc(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
+                       const uint32_t *multiplier, const int8_t *shift, int8_t *y, int64_t M, int64_t K, int64_t N,
+                       void *stream);
+
 #ifdef __cplusplus
 }
 #endif
