@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--decode-runs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=64, help="query rows of the CPU sample")
+    ap.add_argument("--phase", default="all", choices=["all", "encoder", "decoder"],
+                    help="restrict the run (for profiling): encoder only, or decoder only")
     return ap.parse_args()
 
 
@@ -284,6 +286,8 @@ def main():
     enc_gops = enc_gop(dims)
 
     # ---- encoder, device-resident inputs ---------------------------------
+    if args.phase == "decoder":
+        args.steps, args.warmup = 1, 0
     for _ in range(args.warmup):
         model.encoder(mel)
     barrier()
@@ -331,31 +335,36 @@ def main():
     e2e_value = windows / (float(e2e_ms.item()) / 1e3)
 
     # ---- greedy decoder ------------------------------------------------------
+    dec_tps = dec_e2e_tps = float("nan")
+    dec_ms = torch.tensor([float("nan")])
+    if args.phase == "encoder":
+        args.decode_runs = 0
     xa = model.encoder(mel)
     rs_xa = model._enc_ws[B]["rs_xa"]
-    model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)  # warm-up + graph capture
-    barrier()
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record()
-    for _ in range(args.decode_runs):
+    if args.decode_runs > 0:
+        model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)  # warm-up + graph capture
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.decode_runs):
+            toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
+        g1.record()
+        barrier()
+        dec_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(dec_ms, op=dist.ReduceOp.MAX)
+        dec_tokens = B * world * args.decode_tokens * args.decode_runs
+        dec_tps = dec_tokens / (float(dec_ms.item()) / 1e3)
+        h_tok = torch.empty(B, 3 + args.decode_tokens, dtype=torch.int64).pin_memory()
+        g0.record()
         toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
-    g1.record()
-    barrier()
-    dec_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(dec_ms, op=dist.ReduceOp.MAX)
-    dec_tokens = B * world * args.decode_tokens * args.decode_runs
-    dec_tps = dec_tokens / (float(dec_ms.item()) / 1e3)
-    h_tok = torch.empty(B, 3 + args.decode_tokens, dtype=torch.int64).pin_memory()
-    g0.record()
-    toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
-    h_tok.copy_(toks, non_blocking=True)
-    g1.record()
-    barrier()
-    dec_e2e_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(dec_e2e_ms, op=dist.ReduceOp.MAX)
-    dec_e2e_tps = B * world * args.decode_tokens / (float(dec_e2e_ms.item()) / 1e3)
+        h_tok.copy_(toks, non_blocking=True)
+        g1.record()
+        barrier()
+        dec_e2e_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(dec_e2e_ms, op=dist.ReduceOp.MAX)
+        dec_e2e_tps = B * world * args.decode_tokens / (float(dec_e2e_ms.item()) / 1e3)
 
     # ---- roofline of the dominant kernel ------------------------------------
     peaks = measured_peaks()
@@ -392,7 +401,7 @@ def main():
                              "of_datasheet_4500": round(enc_tops / DATASHEET_INT8_TOPS, 4)},
         "decoder": {"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
                     "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
-                    "ms_per_decode": round(float(dec_ms.item()) / args.decode_runs, 2)},
+                    "ms_per_decode": round(float(dec_ms.item()) / max(1, args.decode_runs), 2)},
         "e2e": {"value": round(e2e_value, 3), "unit": "windows/s", "h2d_bytes_per_step": int(h_mel.numel()),
                 "d2h_bytes_per_step": int(h_out.numel())},
         "roofline": roof,
