@@ -246,9 +246,9 @@ int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, in
     if (mask_mode == 2 && !mask) return fail(IW_EINVAL, "iw_attention: mask_mode 2 needs a mask");
     if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
     if (!(rsqrt_offset >= 0 && rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
-    if ((ldq | ldk | ldv | q_bs | k_bs | v_bs) & 15 || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15 ||
-        (reinterpret_cast<uintptr_t>(v) & 1))
-        return fail(IW_EINVAL, "iw_attention: Q/K rows must be 16-byte aligned");
+    if ((ldq | ldk | ldv | q_bs | k_bs | v_bs) & 15 ||
+        (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
+        return fail(IW_EINVAL, "iw_attention: Q/K/V rows must be 16-byte aligned");
     iw::AttnArgs a;
     a.q = q; a.ldq = ldq; a.q_bs = q_bs;
     a.k = k; a.ldk = ldk; a.k_bs = k_bs;
@@ -436,10 +436,10 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream) {
     if (!(d->frac_bits > 0 && d->frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
     if (!(d->rsqrt_offset >= 0 && d->rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
     if (d->mask_mode == 2 && !d->mask) return fail(IW_EINVAL, "iw_attention_ex: mask_mode 2 needs a mask");
-    if (((d->ldq | d->ldk | d->q_bs | d->k_bs | d->q_hs | d->k_hs) & 15) ||
-        ((reinterpret_cast<uintptr_t>(d->q) | reinterpret_cast<uintptr_t>(d->k)) & 15) ||
-        ((d->ldv | d->v_bs | d->v_hs | reinterpret_cast<uintptr_t>(d->v)) & 1))
-        return fail(IW_EINVAL, "iw_attention_ex: Q/K rows must be 16-byte aligned");
+    if (((d->ldq | d->ldk | d->ldv | d->q_bs | d->k_bs | d->v_bs | d->q_hs | d->k_hs | d->v_hs) & 15) ||
+        ((reinterpret_cast<uintptr_t>(d->q) | reinterpret_cast<uintptr_t>(d->k) | reinterpret_cast<uintptr_t>(d->v)) &
+         15))
+        return fail(IW_EINVAL, "iw_attention_ex: Q/K/V rows must be 16-byte aligned");
     iw::AttnArgs a;
     a.q = d->q; a.ldq = d->ldq; a.q_bs = d->q_bs; a.q_hs = d->q_hs;
     a.k = d->k; a.ldk = d->ldk; a.k_bs = d->k_bs; a.k_hs = d->k_hs;

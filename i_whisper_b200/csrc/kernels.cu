@@ -379,88 +379,121 @@ cudaError_t pad_rows(const int8_t *x, int64_t rows, int64_t cols, int8_t *out, i
 // One CTA handles QB query rows of one (batch, head): QK^T + requant +
 // row max (scores kept in shared memory), shift-exp + row sum, P.V,
 // FISR^2 normalisation and the AV requant, written to [B, Tq, H*64].
-// Used for decode-shaped problems (few query rows) where the K/V stream
-// from HBM dominates.
+// Used for decode-shaped problems (few query rows), where streaming K and V
+// from HBM is the whole cost: four lanes share one 64-byte key or value row
+// (one 16-byte load each, so a warp instruction reads eight whole rows),
+// and kAttnU rows per lane are in flight before any arithmetic. A value row
+// whose probabilities are all zero contributes nothing to P.V and is not
+// read at all.
 // ---------------------------------------------------------------------------
 static constexpr int kAttnThreads = 256;
-static constexpr int kAttnQB = 4;
+static constexpr int kAttnWarps = kAttnThreads / 32;
+static constexpr int kAttnU = 4;                   // 64-key groups in flight per lane
+static constexpr int kAttnKeysPerPass = kAttnThreads / 4;
 
+IW_DEV int4 ld_nc_v4(const int8_t *p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// c + sum over the four bytes of (unsigned a_i) * (signed b_i)
+IW_DEV int32_t dp4a_us(uint32_t a, int32_t b, int32_t c) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+template <int QB>
 __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     extern __shared__ uint8_t smem[];
     const int Tk = a.Tk_dev ? *a.Tk_dev : a.Tk;
     const int Tq = a.Tq;
     const int h = blockIdx.y, b = blockIdx.z;
-    const int q0 = blockIdx.x * kAttnQB;
-    const int nq = min(kAttnQB, Tq - q0);
+    const int q0 = blockIdx.x * QB;
+    const int nq = min(QB, Tq - q0);
     if (nq <= 0) return;
-    int16_t *s = reinterpret_cast<int16_t *>(smem);                    // [QB][Tk]
-    uint8_t *pp = reinterpret_cast<uint8_t *>(s + kAttnQB * Tk);        // [QB][Tk]
-    __shared__ int32_t qv[kAttnQB][16];
-    __shared__ int32_t red[kAttnQB][kAttnThreads / 32];
-    __shared__ int32_t rowv[kAttnQB][2];
-    __shared__ int32_t pv_part[kAttnThreads / 32][kAttnQB][64];
+    int16_t *s = reinterpret_cast<int16_t *>(smem);          // [QB][Tk]
+    uint8_t *pp = reinterpret_cast<uint8_t *>(s + QB * Tk);  // [QB][Tk]
+    __shared__ int32_t red[QB][kAttnWarps];
+    __shared__ int32_t rowv[QB][2];
+    __shared__ int32_t pv_part[kAttnWarps][QB][64];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid < kAttnQB * 16) {
-        const int r = tid / 16, w = tid % 16;
-        int32_t val = 0;
-        if (r < nq) {
-            const int8_t *qr = a.q + (int64_t)b * a.q_bs + (int64_t)(q0 + r) * a.ldq + (int64_t)h * a.q_hs;
-            val = reinterpret_cast<const int32_t *>(qr)[w];
-        }
-        qv[r][w] = val;
+    const int sub = lane & 3;                  // which 16 bytes of the 64-byte row
+    const int slot = warp * 8 + (lane >> 2);   // key within a group of kAttnKeysPerPass
+
+    int32_t qv[QB][4];
+#pragma unroll
+    for (int r = 0; r < QB; ++r) {
+        int4 t = make_int4(0, 0, 0, 0);
+        if (r < nq)
+            t = *reinterpret_cast<const int4 *>(a.q + (int64_t)b * a.q_bs + (int64_t)(q0 + r) * a.ldq +
+                                                (int64_t)h * a.q_hs + 16 * sub);
+        qv[r][0] = t.x, qv[r][1] = t.y, qv[r][2] = t.z, qv[r][3] = t.w;
     }
-    __syncthreads();
+
     // pass 1: scores + row max
-    int32_t lmax[kAttnQB];
+    int32_t lmax[QB];
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) lmax[r] = -32768;
+    for (int r = 0; r < QB; ++r) lmax[r] = -32768;
     const uint32_t qsh = (uint32_t)(a.qk_shift > 0 ? a.qk_shift : 0);
-    for (int j = tid; j < Tk; j += kAttnThreads) {
-        const int4 *kr = reinterpret_cast<const int4 *>(a.k + (int64_t)b * a.k_bs + (int64_t)j * a.ldk + (int64_t)h * a.k_hs);
-        int4 kk[4];
+    const int8_t *kb = a.k + (int64_t)b * a.k_bs + (int64_t)h * a.k_hs + 16 * sub;
+    for (int j0 = 0; j0 < Tk; j0 += kAttnU * kAttnKeysPerPass) {
+        int4 kk[kAttnU];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) kk[u] = kr[u];
-        const int32_t *kw = reinterpret_cast<const int32_t *>(kk);
+        for (int u = 0; u < kAttnU; ++u) {
+            const int j = j0 + u * kAttnKeysPerPass + slot;
+            kk[u] = j < Tk ? ld_nc_v4(kb + (int64_t)j * a.ldk) : make_int4(0, 0, 0, 0);
+        }
 #pragma unroll
-        for (int r = 0; r < kAttnQB; ++r) {
-            if (r < nq) {
-                const int qi = Tk - Tq + q0 + r;  // absolute query position
-                bool masked = false;
-                if (a.mask_mode == 1) masked = j > qi;
-                else if (a.mask_mode == 2) masked = a.mask[(int64_t)(q0 + r) * Tk + j] != 0;
-                int16_t sv = -32768;
-                if (!masked) {
-                    int32_t acc = 0;
+        for (int u = 0; u < kAttnU; ++u) {
+            const int j = j0 + u * kAttnKeysPerPass + slot;
 #pragma unroll
-                    for (int w = 0; w < 16; ++w) acc = __dp4a(kw[w], qv[r][w], acc);
-                    int32_t t = rrs(wmul(acc, (int32_t)a.qk_mult), qsh);
-                    sv = (int16_t)clampi(t, -32768, 32767);
-                    lmax[r] = max(lmax[r], (int32_t)sv);
+            for (int r = 0; r < QB; ++r) {
+                int32_t acc = __dp4a(kk[u].x, qv[r][0], 0);
+                acc = __dp4a(kk[u].y, qv[r][1], acc);
+                acc = __dp4a(kk[u].z, qv[r][2], acc);
+                acc = __dp4a(kk[u].w, qv[r][3], acc);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                if (r < nq && j < Tk) {
+                    const int qi = Tk - Tq + q0 + r;  // absolute query position
+                    bool masked = false;
+                    if (a.mask_mode == 1) masked = j > qi;
+                    else if (a.mask_mode == 2) masked = a.mask[(int64_t)(q0 + r) * Tk + j] != 0;
+                    int16_t sv = -32768;
+                    if (!masked) {
+                        const int32_t t = rrs(wmul(acc, (int32_t)a.qk_mult), qsh);
+                        sv = (int16_t)clampi(t, -32768, 32767);
+                        lmax[r] = max(lmax[r], (int32_t)sv);
+                    }
+                    if (sub == (r & 3)) s[r * Tk + j] = sv;
                 }
-                s[r * Tk + j] = sv;
             }
         }
     }
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) {
-        int32_t m = warp_max(lmax[r]);
+    for (int r = 0; r < QB; ++r) {
+        const int32_t m = warp_max(lmax[r]);
         if (lane == 0) red[r][warp] = m;
     }
     __syncthreads();
-    if (tid < kAttnQB) {
+    if (tid < QB) {
         int32_t m = -32768;
-        for (int w = 0; w < kAttnThreads / 32; ++w) m = max(m, red[tid][w]);
+        for (int w = 0; w < kAttnWarps; ++w) m = max(m, red[tid][w]);
         rowv[tid][0] = (int16_t)(m + 1);  // int16 wrap of row max + 1
     }
     __syncthreads();
     // pass 2: shift-exp + row sum
-    int32_t lsum[kAttnQB];
+    int32_t lsum[QB];
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) lsum[r] = 0;
+    for (int r = 0; r < QB; ++r) lsum[r] = 0;
     for (int j = tid; j < Tk; j += kAttnThreads) {
 #pragma unroll
-        for (int r = 0; r < kAttnQB; ++r) {
+        for (int r = 0; r < QB; ++r) {
             if (r < nq) {
                 const int qi = Tk - Tq + q0 + r;
                 bool masked = false;
@@ -473,44 +506,75 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
         }
     }
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) {
-        int32_t v = warp_sum(lsum[r]);
+    for (int r = 0; r < QB; ++r) {
+        const int32_t v = warp_sum(lsum[r]);
         if (lane == 0) red[r][warp] = v;
     }
     __syncthreads();
-    if (tid < kAttnQB) {
+    if (tid < QB) {
         int32_t v = 0;
-        for (int w = 0; w < kAttnThreads / 32; ++w) v += red[tid][w];
+        for (int w = 0; w < kAttnWarps; ++w) v += red[tid][w];
         rowv[tid][1] = v;
     }
-    // pass 3: P.V. Warp w takes keys w, w+8, ...; lane owns dims 2l, 2l+1.
-    uint32_t acc[kAttnQB][2];
+    // pass 3: P.V, lane (slot, sub) accumulating dims 16*sub .. 16*sub+15.
+    int32_t acc[QB][16];
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) acc[r][0] = acc[r][1] = 0;
-    const int8_t *vb = a.v + (int64_t)b * a.v_bs + (int64_t)h * a.v_hs + 2 * lane;
-    for (int j = warp; j < Tk; j += kAttnThreads / 32) {
-        const int16_t vv = *reinterpret_cast<const int16_t *>(vb + (int64_t)j * a.ldv);
-        const int32_t v0 = (int8_t)(vv & 0xFF), v1 = (int8_t)((vv >> 8) & 0xFF);
+    for (int r = 0; r < QB; ++r)
 #pragma unroll
-        for (int r = 0; r < kAttnQB; ++r) {
-            const int32_t p = pp[r * Tk + j];
-            acc[r][0] += (uint32_t)(p * v0);
-            acc[r][1] += (uint32_t)(p * v1);
+        for (int e = 0; e < 16; ++e) acc[r][e] = 0;
+    const int8_t *vb = a.v + (int64_t)b * a.v_bs + (int64_t)h * a.v_hs + 16 * sub;
+    for (int j0 = 0; j0 < Tk; j0 += kAttnU * kAttnKeysPerPass) {
+        int4 vv[kAttnU];
+        uint32_t pw[kAttnU][QB];
+#pragma unroll
+        for (int u = 0; u < kAttnU; ++u) {
+            const int j = j0 + u * kAttnKeysPerPass + slot;
+            uint32_t any = 0;
+#pragma unroll
+            for (int r = 0; r < QB; ++r) {
+                pw[u][r] = (j < Tk && r < nq) ? (uint32_t)pp[r * Tk + j] : 0u;
+                any |= pw[u][r];
+            }
+            vv[u] = any ? ld_nc_v4(vb + (int64_t)j * a.ldv) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kAttnU; ++u) {
+            const int32_t w4[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+            for (int r = 0; r < QB; ++r) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        acc[r][4 * w + e] = dp4a_us(pw[u][r] << (8 * e), w4[w], acc[r][4 * w + e]);
+            }
         }
     }
+    // reduce over the eight key slots of the warp (lanes with equal sub)
 #pragma unroll
-    for (int r = 0; r < kAttnQB; ++r) {
-        pv_part[warp][r][2 * lane] = (int32_t)acc[r][0];
-        pv_part[warp][r][2 * lane + 1] = (int32_t)acc[r][1];
+    for (int r = 0; r < QB; ++r)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            int32_t v = acc[r][e];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            acc[r][e] = v;
+        }
+    if (lane < 4) {
+#pragma unroll
+        for (int r = 0; r < QB; ++r)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pv_part[warp][r][16 * sub + e] = acc[r][e];
     }
     __syncthreads();
     const uint32_t avs = (uint32_t)clampi(a.av_shift, 0, 32);
-    for (int idx = tid; idx < kAttnQB * 64; idx += kAttnThreads) {
+    for (int idx = tid; idx < QB * 64; idx += kAttnThreads) {
         const int r = idx / 64, d = idx % 64;
         if (r >= nq) continue;
         uint32_t sum = 0;
 #pragma unroll
-        for (int w = 0; w < kAttnThreads / 32; ++w) sum += (uint32_t)pv_part[w][r][d];
+        for (int w = 0; w < kAttnWarps; ++w) sum += (uint32_t)pv_part[w][r][d];
         const int32_t inv = fisr(rowv[r][1], a.rsqrt_offset);
         int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
         v = rrs(wmul(v, inv), a.rsqrt_offset);
@@ -519,19 +583,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     }
 }
 
-cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
-    if (B <= 0 || H <= 0 || a.Tq <= 0) return cudaSuccess;
+template <int QB>
+static cudaError_t attention_cc_launch(const AttnArgs &a, int B, int H, cudaStream_t st) {
     const int tk_cap = a.Tk_cap > 0 ? a.Tk_cap : a.Tk;
-    const size_t smem = (size_t)kAttnQB * tk_cap * 3;
+    const size_t smem = (size_t)QB * tk_cap * 3;
     static size_t smem_set = 0;
     if (smem > 48 * 1024 && smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_cc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(attn_cc_kernel<QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
-    dim3 grid((a.Tq + kAttnQB - 1) / kAttnQB, H, B);
-    attn_cc_kernel<<<grid, kAttnThreads, smem, st>>>(a);
+    dim3 grid((a.Tq + QB - 1) / QB, H, B);
+    attn_cc_kernel<QB><<<grid, kAttnThreads, smem, st>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
+    if (B <= 0 || H <= 0 || a.Tq <= 0) return cudaSuccess;
+    // one query row per CTA for decode steps; four otherwise (each CTA
+    // re-reads K and V of its head, so wider query blocks save traffic)
+    return a.Tq <= 2 ? attention_cc_launch<1>(a, B, H, st) : attention_cc_launch<4>(a, B, H, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,0 +1,209 @@
+"""Kernel microbenchmark of the integer hot path (the seeded kernel shapes of
+the reference's benchmark configuration: w8a8 GEMM at M = 1500*B, integer
+LayerNorm over 1500 x 1024 rows, 16-head 1500 x 1500 integer attention) plus
+the decode-shaped attention over a 1500-position cross-attention cache.
+
+Every case runs through the C ABI on preallocated device buffers, is timed
+with CUDA events on the launching stream after warm-up, and prints one JSON
+line with its roofline fraction. It is also the command the committed ncu
+summaries are taken with (small cases, one kernel per process).
+
+    python -m i_whisper_b200.microbench gemm --M 12000 --K 1024 --N 4096
+    python -m i_whisper_b200.microbench layernorm --rows 1500 --d 1024
+    python -m i_whisper_b200.microbench attention --B 4 --H 16 --T 1500
+    python -m i_whisper_b200.microbench cross_attention --B 256 --H 16 --T 1500
+
+Input distributions follow the benchmark configuration: INT8 entries uniform
+in [-127, 127]; per-channel scales uniform in [1e-3, 1e-2] turned into
+(u32 multiplier, shift) by the frexp rule of the quantiser; attention Q/K/V
+from clamp(round(N(0, 30)), +-127).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+
+import numpy as np
+import torch
+
+from . import _lib
+from .checkpoint import _frexp_u32
+
+DATASHEET_INT8_TOPS = 4500.0
+
+
+def hbm_peak():
+    """(GB/s, source): the measured copy bandwidth of this GPU pool when the
+    peaks file is present next to the package, else the earlier fallback."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def _time(fn, reps: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(reps):
+        fn()
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _i8(g: torch.Generator, *shape) -> torch.Tensor:
+    return torch.randint(-127, 128, shape, dtype=torch.int8, generator=g).cuda()
+
+
+def _gauss_i8(g: torch.Generator, *shape) -> torch.Tensor:
+    return torch.clamp(torch.round(torch.randn(shape, generator=g) * 30.0), -127, 127).to(torch.int8).cuda()
+
+
+def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: int) -> dict:
+    g = torch.Generator().manual_seed(seed)
+    x, w = _i8(g, M, K), _i8(g, N, K)
+    rng = np.random.default_rng(seed)
+    m, s = _frexp_u32(rng.uniform(1e-3, 1e-2, N))
+    mult = torch.from_numpy(m.astype(np.uint32)).cuda()
+    shift = torch.from_numpy(s.astype(np.int8)).cuda()
+    bias = torch.from_numpy(rng.integers(-2**20, 2**20, N).astype(np.int32)).cuda()
+    wz = torch.from_numpy(rng.integers(-8, 8, N).astype(np.int8)).cuda()
+    rs = torch.empty(M, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.call("iw_rowsum_i8", x.data_ptr(), K, M, K, rs.data_ptr(), stream)
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = x.data_ptr(), K, w.data_ptr(), K, M, N, K
+    d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = (bias.data_ptr(), wz.data_ptr(), rs.data_ptr(),
+                                                               mult.data_ptr(), shift.data_ptr())
+    d.tile_n = tile_n
+    keep = [x, w, mult, shift, bias, wz, rs]
+    if mode == "linear8":
+        out = torch.empty(M, N, dtype=torch.int8, device="cuda")
+        d.mode = _lib.IW_GEMM_INT8
+        out_bytes = M * N
+    else:  # linear32 + residual15 (out-projection / fc2)
+        out = torch.empty(M, N, dtype=torch.int16, device="cuda")
+        res = torch.randint(-16383, 16384, (M, N), dtype=torch.int16, generator=g).cuda()
+        keep.append(res)
+        d.mode = _lib.IW_GEMM_LINEAR32_RES
+        d.residual, d.ldr, d.residual_multiplier = res.data_ptr(), N, 23000
+        out_bytes = 4 * M * N
+    d.out, d.ldo = out.data_ptr(), N
+    ms = _time(lambda: _lib.check(_lib.LIB.iw_gemm_i8(C.byref(d), stream)), reps)
+    tops = 2.0 * M * N * K / ms / 1e9
+    return {"op": "gemm", "mode": mode, "M": M, "K": K, "N": N, "tile_n": tile_n, "ms": round(ms, 4),
+            "tops": round(tops, 1), "frac_of_datasheet_4500": round(tops / DATASHEET_INT8_TOPS, 4),
+            "algorithmic_bytes": M * K + N * K + out_bytes}
+
+
+def bench_layernorm(rows: int, d: int, reps: int, seed: int) -> dict:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randint(-16383, 16384, (rows, d), dtype=torch.int16, generator=g).cuda()
+    gamma = _i8(g, d)
+    beta = torch.randint(-2**15, 2**15, (d,), dtype=torch.int32, generator=g).cuda()
+    y = torch.empty(rows, d, dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    ms = _time(lambda: _lib.call("iw_layernorm32", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), 180, 9,
+                                 1 << 30, 18, y.data_ptr(), rows, d, stream), reps)
+    hbm, src = hbm_peak()
+    gbs = rows * d * 3 / ms / 1e6
+    return {"op": "layernorm32", "rows": rows, "d": d, "ms": round(ms, 4), "gbs": round(gbs, 1),
+            "frac": round(gbs / hbm, 4), "peak_gbs": hbm, "peak_source": src}
+
+
+def _attn_desc(q, ldq, q_bs, q_hs, k, ldk, k_bs, k_hs, v, ldv, v_bs, v_hs, y, ldy, y_bs, B, H, Tq, Tk):
+    a = _lib.AttnDesc()
+    a.q, a.ldq, a.q_bs, a.q_hs = q, ldq, q_bs, q_hs
+    a.k, a.ldk, a.k_bs, a.k_hs = k, ldk, k_bs, k_hs
+    a.v, a.ldv, a.v_bs, a.v_hs = v, ldv, v_bs, v_hs
+    a.y, a.ldy, a.y_bs, a.y_hs = y, ldy, y_bs, 64
+    a.B, a.H, a.Tq, a.Tk = B, H, Tq, Tk
+    a.qk_multiplier, a.qk_shift, a.frac_bits = 182, 12, 7
+    a.av_multiplier, a.av_shift, a.rsqrt_offset = 192, 7, 16
+    return a
+
+
+def bench_attention(B: int, H: int, T: int, reps: int, seed: int) -> dict:
+    """Encoder self-attention straight from a fused QKV projection buffer."""
+    g = torch.Generator().manual_seed(seed)
+    d = H * 64
+    qkv = _gauss_i8(g, B * T, 3 * d)
+    out = torch.empty(B * T, d, dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    tab = torch.empty(32772, dtype=torch.uint8, device="cuda")
+    _lib.call("iw_shift_exp_table", 7, tab.data_ptr(), stream)
+    vt_ld = (T + 15) // 16 * 16
+    vt = torch.empty(B * H * 64, vt_ld, dtype=torch.int8, device="cuda")
+    base = qkv.data_ptr()
+    a = _attn_desc(base, 3 * d, T * 3 * d, 64, base + d, 3 * d, T * 3 * d, 64, base + 2 * d, 3 * d, T * 3 * d, 64,
+                   out.data_ptr(), d, T * d, B, H, T, T)
+    a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
+    ms = _time(lambda: _lib.check(_lib.LIB.iw_attention_ex(C.byref(a), stream)), reps)
+    tops = 4.0 * B * H * T * T * 64 / ms / 1e9
+    return {"op": "attention", "B": B, "H": H, "T": T, "ms": round(ms, 4), "tops": round(tops, 1),
+            "frac_of_datasheet_4500": round(tops / DATASHEET_INT8_TOPS, 4),
+            "note": "ops count QK^T and P.V once (the kernel computes QK^T twice)"}
+
+
+def bench_cross_attention(B: int, H: int, T: int, reps: int, seed: int) -> dict:
+    """One decode step of cross-attention: one query row per utterance over
+    a head-major [H, B, T, 64] INT8 key cache and value cache."""
+    g = torch.Generator().manual_seed(seed)
+    d = H * 64
+    q = _gauss_i8(g, B, d)
+    k = _gauss_i8(g, H, B, T, 64)
+    v = _gauss_i8(g, H, B, T, 64)
+    out = torch.empty(B, d, dtype=torch.int8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    a = _attn_desc(q.data_ptr(), d, d, 64, k.data_ptr(), 64, T * 64, B * T * 64, v.data_ptr(), 64, T * 64,
+                   B * T * 64, out.data_ptr(), d, d, B, H, 1, T)
+    ms = _time(lambda: _lib.check(_lib.LIB.iw_attention_ex(C.byref(a), stream)), reps)
+    hbm, src = hbm_peak()
+    nbytes = 2 * B * H * T * 64
+    gbs = nbytes / ms / 1e6
+    return {"op": "cross_attention", "B": B, "H": H, "Tk": T, "ms": round(ms, 4), "gbs": round(gbs, 1),
+            "frac": round(gbs / hbm, 4), "peak_gbs": hbm, "peak_source": src, "algorithmic_bytes": nbytes}
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    p.add_argument("op", choices=["gemm", "layernorm", "attention", "cross_attention"])
+    p.add_argument("--M", type=int, default=12000)
+    p.add_argument("--K", type=int, default=1024)
+    p.add_argument("--N", type=int, default=4096)
+    p.add_argument("--mode", choices=["linear8", "linear32_residual15"], default="linear8")
+    p.add_argument("--tile-n", type=int, default=0, help="GEMM N tile (0: library choice)")
+    p.add_argument("--rows", type=int, default=1500)
+    p.add_argument("--d", type=int, default=1024)
+    p.add_argument("--B", type=int, default=4)
+    p.add_argument("--H", type=int, default=16)
+    p.add_argument("--T", type=int, default=1500)
+    p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--seed", type=int, default=0)
+    a = p.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("microbench needs a CUDA device")
+    torch.cuda.set_device(0)
+    if a.op == "gemm":
+        r = bench_gemm(a.M, a.K, a.N, a.mode, a.tile_n, a.reps, a.seed)
+    elif a.op == "layernorm":
+        r = bench_layernorm(a.rows, a.d, a.reps, a.seed)
+    elif a.op == "attention":
+        r = bench_attention(a.B, a.H, a.T, a.reps, a.seed)
+    else:
+        r = bench_cross_attention(a.B, a.H, a.T, a.reps, a.seed)
+    if _lib.device_status(clear=True) != 0:
+        raise SystemExit("a device-side wait timed out")
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

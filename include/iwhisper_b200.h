@@ -123,7 +123,8 @@ int iw_pv_norm_requant(const uint8_t *p, const int8_t *v, const int32_t *row_sum
  * (same for K, V with their strides); y[b*y_bs + t*ldy + h*64 + d].
  * mask_mode 0: none, 1: causal (key j masked when j > Tk-Tq+i, the slice of
  * TextDecoder_int.mask taken at model_int.py:786-799), 2: explicit mask
- * [Tq,Tk]. Encoder-sized problems run on the tensor cores. */
+ * [Tq,Tk]. q, k, v and their row and batch strides must be multiples of
+ * 16 bytes (IW_EINVAL otherwise). */
 int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, int64_t ldk, int64_t k_bs,
                  const int8_t *v, int64_t ldv, int64_t v_bs, int8_t *y, int64_t ldy, int64_t y_bs, int64_t B,
                  int64_t H, int64_t Tq, int64_t Tk, int mask_mode, const uint8_t *mask, uint8_t qk_multiplier,
