@@ -514,6 +514,8 @@ int iw_kv_append(const int8_t *src, int64_t lds, int64_t k_col, int64_t v_col, i
 
 int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream) {
     if (!d) return fail(IW_EINVAL, "iw_greedy_step: null descriptor");
+    if (d->V <= 0 || d->ld < d->V || d->V > INT32_MAX) return fail(IW_EINVAL, "iw_greedy_step: need 0 < V <= ld");
+    if (!(d->alpha > 0.f)) return fail(IW_EINVAL, "iw_greedy_step: alpha must be positive");
     iw::GreedyArgs g;
     g.logits = d->logits; g.ld = d->ld; g.V = (int)d->V; g.alpha = d->alpha;
     g.suppress_bits = d->suppress_bits; g.blank = d->blank; g.n_blank = (int)d->n_blank;

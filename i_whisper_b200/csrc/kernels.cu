@@ -645,18 +645,7 @@ cudaError_t kv_append(const int8_t *src, int64_t lds, int k_col, int v_col, int8
 // (decoding.py:280-296): first index of the maximum, EOT kept once emitted.
 // One CTA per utterance.
 // ---------------------------------------------------------------------------
-static constexpr int kGreedyThreads = 1024;
-
-IW_DEV float block_reduce_max(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float r = -INFINITY;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
-    return r;
-}
+static constexpr int kGreedyThreads = 512;
 
 IW_DEV float block_reduce_sum(float v, float *red) {
 #pragma unroll
@@ -669,11 +658,38 @@ IW_DEV float block_reduce_sum(float v, float *red) {
     return r;
 }
 
+// Best (largest int8 logit, then smallest index) of two candidates.
+IW_DEV void best_merge(int &q, int &i, int oq, int oi) {
+    if (oq > q || (oq == q && oi < i)) { q = oq; i = oi; }
+}
+
+IW_DEV void block_best(int &q, int &i, int *qred, int *ired) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) best_merge(q, i, __shfl_xor_sync(0xffffffffu, q, o), __shfl_xor_sync(0xffffffffu, i, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) { qred[threadIdx.x >> 5] = q; ired[threadIdx.x >> 5] = i; }
+    __syncthreads();
+    q = qred[0], i = ired[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best_merge(q, i, qred[w], ired[w]);
+}
+
+// One greedy step per utterance (GreedyDecoder.update after the logit
+// filters SuppressBlank, SuppressTokens and ApplyTimestampRules,
+// decoding.py:280-296 and 426-510). The logits are INT8 values q scaled by
+// 1/alpha (alpha > 0), so the float logit is a monotone function of q and
+// the log-softmax sums of ApplyTimestampRules need only a histogram of the
+// 256 possible values: one pass over the row gathers, for the tokens no
+// rule suppresses, the histogram of all of them and of the timestamp
+// tokens, and the best text and best timestamp token (largest q, then
+// smallest index, as torch.argmax). Every log-probability is then formed
+// with the same float operations as the per-token formula.
 __global__ void __launch_bounds__(kGreedyThreads) greedy_step_kernel(GreedyArgs g) {
     const int b = blockIdx.x;
     const int tid = threadIdx.x;
+    __shared__ uint32_t hist[2][256];  // [0]: every allowed token, [1]: allowed timestamp tokens
     __shared__ float red[32];
-    __shared__ int32_t ired[32];
+    __shared__ int qred[32], ired[32];
+    for (int i = tid; i < 512; i += kGreedyThreads) hist[i >> 8][i & 255] = 0;
     int32_t *st = g.state + 4 * b;
     const int n = st[0], last = st[1], pen = st[2], last_ts_val = st[3];
     const int tb = g.timestamp_begin;
@@ -683,78 +699,74 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_step_kernel(GreedyArgs 
     int ts_hi = -1;  // timestamps in [tb, ts_hi) are forbidden
     if (last_ts_val >= 0) ts_hi = (last_ts && !pen_ts) ? last_ts_val : last_ts_val + 1;
     const int8_t *lg = g.logits + (int64_t)b * g.ld;
-    // masked logit value: q/alpha, -inf where a rule suppresses the token
-    auto masked_val = [&](int i) -> float {
+    auto allowed = [&](int i) -> bool {
         if (at_begin) {
-            if (i == g.eot) return -INFINITY;
+            if (i == g.eot) return false;
             for (int u = 0; u < g.n_blank; ++u)
-                if (g.blank[u] == i) return -INFINITY;
+                if (g.blank[u] == i) return false;
         }
-        if ((g.suppress_bits[i >> 5] >> (i & 31)) & 1u) return -INFINITY;
-        if (i == g.no_timestamps) return -INFINITY;
+        if ((g.suppress_bits[i >> 5] >> (i & 31)) & 1u) return false;
+        if (i == g.no_timestamps) return false;
         if (last_ts) {
             if (pen_ts) {
-                if (i >= tb) return -INFINITY;
+                if (i >= tb) return false;
             } else if (i < g.eot) {
-                return -INFINITY;
+                return false;
             }
         }
-        if (i >= tb && i < ts_hi) return -INFINITY;
+        if (i >= tb && i < ts_hi) return false;
         if (at_begin) {
-            if (i < tb) return -INFINITY;
-            if (g.max_initial_timestamp_index >= 0 && i > tb + g.max_initial_timestamp_index) return -INFINITY;
+            if (i < tb) return false;
+            if (g.max_initial_timestamp_index >= 0 && i > tb + g.max_initial_timestamp_index) return false;
         }
-        return (float)lg[i] / g.alpha;
+        return true;
     };
-    // log_softmax over the masked logits
-    float mx = -INFINITY;
-    for (int i = tid; i < g.V; i += kGreedyThreads) mx = fmaxf(mx, masked_val(i));
-    mx = block_reduce_max(mx, red);
+    __syncthreads();
+    int tq = -1000, ti = 0x7fffffff;  // best text token
+    int sq = -1000, si = 0x7fffffff;  // best timestamp token
+    for (int i = tid; i < g.V; i += kGreedyThreads) {
+        if (!allowed(i)) continue;
+        const int q = lg[i];
+        atomicAdd(&hist[0][q + 128], 1u);
+        if (i >= tb) {
+            atomicAdd(&hist[1][q + 128], 1u);
+            if (q > sq) sq = q, si = i;
+        } else if (q > tq) {
+            tq = q, ti = i;
+        }
+    }
+    block_best(tq, ti, qred, ired);
+    block_best(sq, si, qred, ired);
+    const bool any_text = ti != 0x7fffffff, any_ts = si != 0x7fffffff;
+    // log_softmax over the allowed logits
+    const float mx = (!any_text && !any_ts) ? -INFINITY : (float)max(any_text ? tq : -1000, any_ts ? sq : -1000) / g.alpha;
     float se = 0.f;
-    for (int i = tid; i < g.V; i += kGreedyThreads) se += expf(masked_val(i) - mx);
+    float vbin = 0.f;
+    uint32_t c_all = 0, c_ts = 0;
+    if (tid < 256) {
+        vbin = (float)(tid - 128) / g.alpha;
+        c_all = hist[0][tid];
+        c_ts = hist[1][tid];
+        if (c_all) se = (float)c_all * expf(vbin - mx);
+    }
     se = block_reduce_sum(se, red);
     const float lse = logf(se);
-    // timestamp mass vs. best text token (decoding.py:500-510)
-    float m2 = -INFINITY, mt = -INFINITY;
-    for (int i = tid; i < g.V; i += kGreedyThreads) {
-        const float lp = masked_val(i) - mx - lse;
-        if (i >= tb) m2 = fmaxf(m2, lp);
-        else mt = fmaxf(mt, lp);
-    }
-    m2 = block_reduce_max(m2, red);
-    mt = block_reduce_max(mt, red);
+    // timestamp mass against the best text token (decoding.py:500-510)
+    const float m2 = any_ts ? (float)sq / g.alpha - mx - lse : -INFINITY;
+    const float mt = any_text ? (float)tq / g.alpha - mx - lse : -INFINITY;
     float s2 = 0.f;
-    if (m2 != -INFINITY)
-        for (int i = tb + tid; i < g.V; i += kGreedyThreads) s2 += expf((masked_val(i) - mx - lse) - m2);
+    if (tid < 256 && any_ts && c_ts) s2 = (float)c_ts * expf((vbin - mx - lse) - m2);
     s2 = block_reduce_sum(s2, red);
-    const float ts_lp = (m2 == -INFINITY) ? -INFINITY : m2 + logf(s2);
+    const float ts_lp = any_ts ? m2 + logf(s2) : -INFINITY;
     const bool force_ts = ts_lp > mt;
-    // argmax (first index of the maximum)
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = tid; i < g.V; i += kGreedyThreads) {
-        float v = masked_val(i);
-        if (force_ts && i < tb) v = -INFINITY;
-        if (v > best || (v == best && i < bi)) { best = v; bi = i; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    __syncthreads();
-    if ((tid & 31) == 0) { red[tid >> 5] = best; ired[tid >> 5] = bi; }
-    __syncthreads();
     if (tid == 0) {
-        float bv = red[0];
-        int bidx = ired[0];
-        for (int w = 1; w < kGreedyThreads / 32; ++w)
-            if (red[w] > bv || (red[w] == bv && ired[w] < bidx)) { bv = red[w]; bidx = ired[w]; }
+        int bq = -1000, bidx = 0x7fffffff;
+        if (!force_ts) best_merge(bq, bidx, tq, ti);
+        best_merge(bq, bidx, sq, si);
         if (bidx == 0x7fffffff) bidx = 0;
         const int col = *g.step_dev;
         const int64_t prev = g.tokens[(int64_t)b * g.ld_tok + col - 1];
-        int64_t nxt = (prev == g.eot) ? (int64_t)g.eot : (int64_t)bidx;
+        const int64_t nxt = (prev == g.eot) ? (int64_t)g.eot : (int64_t)bidx;
         g.tokens[(int64_t)b * g.ld_tok + col] = nxt;
         g.next[b] = nxt;
         st[0] = n + 1;

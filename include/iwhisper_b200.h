@@ -304,7 +304,9 @@ typedef struct iw_greedy_desc {
 
 /* One greedy decoding step on the device: SuppressBlank, SuppressTokens,
  * ApplyTimestampRules (decoding.py:426-510) and GreedyDecoder.update
- * (decoding.py:280-296). */
+ * (decoding.py:280-296). logits rows hold the int8 logits q of V tokens
+ * at stride ld >= V; the float logit is q / alpha with alpha > 0
+ * (IW_EINVAL otherwise). */
 int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream);
 
 /* *p += v on the device (advances device-side decode counters). */

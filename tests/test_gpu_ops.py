@@ -378,3 +378,73 @@ def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
     _lib.check(_lib.LIB.iw_attention_ex(ctypes.byref(a), st))
     assert np.array_equal(host(out).reshape(B, T, d), ref)
     assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("n_hist", [0, 1, 2, 3, 5])
+def test_greedy_step(n_hist):
+    """iw_greedy_step against the oracle's filter chain + argmax on random
+    INT8 logits, for token histories of every kind (text, timestamps, pairs,
+    EOT), with logit rows at a padded stride."""
+    import ctypes as C
+    from i_whisper_b200 import _lib
+    from i_whisper_b200.model import decode_tokens
+    V, B = 51865, 48
+    ld = (V + 31) // 32 * 32
+    t = decode_tokens(V)
+    tb, eot = t["timestamp_begin"], t["eot"]
+    spec = O.DecodeTokens(sot=t["sot"], eot=eot, sot_sequence=t["sot_sequence"], no_timestamps=t["no_timestamps"],
+                          timestamp_begin=tb, blank=t["blank"], suppress=t["suppress"])
+    rng = np.random.default_rng(100 + n_hist)
+    alpha = 2.5
+    logits = rng.integers(-128, 128, (B, ld), dtype=np.int8)
+    # a third of the rows with a strong timestamp block, so both branches
+    # of the timestamp-mass rule are taken
+    logits[::3, tb:tb + 40] = rng.integers(90, 128, (len(logits[::3]), 40), dtype=np.int8)
+    sot = list(t["sot_sequence"])
+    Tp = len(sot)
+    hist = np.zeros((B, n_hist), np.int64)
+    for b in range(B):
+        for j in range(n_hist):
+            r = rng.random()
+            hist[b, j] = (tb + int(rng.integers(0, 1500))) if r < 0.45 else (eot if r < 0.55 else int(rng.integers(0, eot)))
+    tokens = np.zeros((B, Tp + n_hist + 1), np.int64)
+    tokens[:, :Tp] = sot
+    tokens[:, Tp:Tp + n_hist] = hist
+    state = np.zeros((B, 4), np.int32)
+    state[:, 0] = n_hist
+    state[:, 3] = -1
+    for b in range(B):
+        if n_hist >= 1:
+            state[b, 1] = hist[b, -1]
+        if n_hist >= 2:
+            state[b, 2] = hist[b, -2]
+        ts = [x for x in hist[b] if x >= tb]
+        if ts:
+            state[b, 3] = ts[-1]
+    # expected: the reference filter chain on float logits q / alpha
+    lg = torch.from_numpy(logits[:, :V].astype(np.float32)).div(torch.tensor([alpha], dtype=torch.float32))
+    tt = torch.from_numpy(tokens[:, :Tp + n_hist])
+    O.apply_filters_torch(lg, tt, spec, Tp)
+    want = lg.argmax(dim=-1)
+    want[tt[:, -1] == eot] = eot
+    d_logits, d_tokens, d_state = dev(logits), dev(tokens), dev(state)
+    bits = np.zeros((V + 31) // 32, np.uint32)
+    for s in t["suppress"]:
+        bits[s >> 5] |= np.uint32(1 << (s & 31))
+    d_bits, d_blank = dev(bits), dev(np.array(t["blank"], np.int32))
+    d_step = dev(np.array([Tp + n_hist], np.int32))
+    d_next = torch.zeros(B, dtype=torch.int64, device="cuda")
+    g = _lib.GreedyDesc()
+    g.logits, g.ld, g.V, g.alpha = d_logits.data_ptr(), ld, V, alpha
+    g.suppress_bits, g.blank, g.n_blank = d_bits.data_ptr(), d_blank.data_ptr(), d_blank.numel()
+    g.eot, g.timestamp_begin, g.no_timestamps = eot, tb, t["no_timestamps"]
+    g.max_initial_timestamp_index = 50
+    g.state, g.tokens, g.ld_tok = d_state.data_ptr(), d_tokens.data_ptr(), tokens.shape[1]
+    g.step_dev, g.next = d_step.data_ptr(), d_next.data_ptr()
+    _lib.check(_lib.LIB.iw_greedy_step(C.byref(g), B, torch.cuda.current_stream().cuda_stream))
+    got = host(d_next)
+    assert np.array_equal(got, want.numpy())
+    assert np.array_equal(host(d_tokens)[:, Tp + n_hist], want.numpy())
+    st = host(d_state)
+    assert np.array_equal(st[:, 0], np.full(B, n_hist + 1))
+    assert np.array_equal(st[:, 1], want.numpy())
