@@ -256,6 +256,7 @@ def main():
     import torch.distributed as dist
     from i_whisper_b200.checkpoint import DIMS, synthetic_state_dict
     from i_whisper_b200.model import KernelTimer, WhisperIntB200
+    from i_whisper_b200.sharding import max_over_ranks, shard_bounds, window_seeds
     from i_whisper_b200.synthetic import synthetic_mel_batch
 
     # CPU baseline processes are spawned before this process touches the GPU
@@ -266,7 +267,7 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     def barrier():
         if world > 1:
@@ -279,7 +280,8 @@ def main():
     sd = synthetic_state_dict(dims, seed=0)
     model = WhisperIntB200(dims, sd)
     del sd
-    seeds = [(rank * B + i) % 32 for i in range(B)]
+    start, stop = shard_bounds(B * world, world, rank)  # weak scaling: B utterances per rank
+    seeds = window_seeds(start, stop)
     mels32 = synthetic_mel_batch(dims.n_mels, sorted(set(seeds)), 100.0)
     mel_np = np.stack([mels32[s % len(mels32)] for s in seeds])
     mel = torch.from_numpy(mel_np).cuda()
@@ -306,10 +308,7 @@ def main():
     enc_ms = e0.elapsed_time(e1)
     launches = (model.launches - launches0)
     ksum = timer.summary()
-    t_max = torch.tensor([enc_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    enc_ms = float(t_max.item())
+    enc_ms = max_over_ranks(enc_ms, device="cuda")
     windows = B * world * args.steps
     value = windows / (enc_ms / 1e3)
     ms_per_step = enc_ms / args.steps
@@ -329,14 +328,12 @@ def main():
         h_out.copy_(xa, non_blocking=True)
     f1.record()
     barrier()
-    e2e_ms = torch.tensor([f0.elapsed_time(f1)], device="cuda")
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = windows / (float(e2e_ms.item()) / 1e3)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), device="cuda")
+    e2e_value = windows / (e2e_ms / 1e3)
 
     # ---- greedy decoder ------------------------------------------------------
     dec_tps = dec_e2e_tps = float("nan")
-    dec_ms = torch.tensor([float("nan")])
+    dec_ms = float("nan")
     if args.phase == "encoder":
         args.decode_runs = 0
     xa = model.encoder(mel)
@@ -350,21 +347,17 @@ def main():
             toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
         g1.record()
         barrier()
-        dec_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
-        if world > 1:
-            dist.all_reduce(dec_ms, op=dist.ReduceOp.MAX)
+        dec_ms = max_over_ranks(g0.elapsed_time(g1), device="cuda")
         dec_tokens = B * world * args.decode_tokens * args.decode_runs
-        dec_tps = dec_tokens / (float(dec_ms.item()) / 1e3)
+        dec_tps = dec_tokens / (dec_ms / 1e3)
         h_tok = torch.empty(B, 3 + args.decode_tokens, dtype=torch.int64).pin_memory()
         g0.record()
         toks = model.decode(xa, rs_xa, args.decode_tokens, use_graph=True)
         h_tok.copy_(toks, non_blocking=True)
         g1.record()
         barrier()
-        dec_e2e_ms = torch.tensor([g0.elapsed_time(g1)], device="cuda")
-        if world > 1:
-            dist.all_reduce(dec_e2e_ms, op=dist.ReduceOp.MAX)
-        dec_e2e_tps = B * world * args.decode_tokens / (float(dec_e2e_ms.item()) / 1e3)
+        dec_e2e_ms = max_over_ranks(g0.elapsed_time(g1), device="cuda")
+        dec_e2e_tps = B * world * args.decode_tokens / (dec_e2e_ms / 1e3)
 
     # ---- roofline of the dominant kernel ------------------------------------
     peaks = measured_peaks()
@@ -401,7 +394,7 @@ def main():
                              "of_datasheet_4500": round(enc_tops / DATASHEET_INT8_TOPS, 4)},
         "decoder": {"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
                     "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
-                    "ms_per_decode": round(float(dec_ms.item()) / max(1, args.decode_runs), 2)},
+                    "ms_per_decode": round(dec_ms / max(1, args.decode_runs), 2)},
         "e2e": {"value": round(e2e_value, 3), "unit": "windows/s", "h2d_bytes_per_step": int(h_mel.numel()),
                 "d2h_bytes_per_step": int(h_out.numel())},
         "roofline": roof,

@@ -1,5 +1,5 @@
 // iw_sm100.cuh -- thin inline-PTX wrappers for the Blackwell (sm_100a)
-// features the kernels use: mbarriers, TMA tile loads (no multicast),
+// features the kernels use: mbarriers, TMA tile loads into this CTA only,
 // tcgen05 MMA / TMEM allocation / TMEM loads, and the shared-memory and
 // instruction descriptors of tcgen05.mma kind::i8.
 //
@@ -65,7 +65,7 @@ IW_DEV bool mbar_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
-// ---- TMA (tile mode, no multicast) -----------------------------------------
+// ---- TMA (tile mode, one destination CTA) ----------------------------------
 IW_DEV void tma_load_2d(const CUtensorMap *map, uint64_t *bar, void *dst, int32_t x, int32_t y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
