@@ -75,6 +75,7 @@ class GemmDesc(C.Structure):
         ("pos", _P), ("pos_T", _I64), ("pos_multiplier", _P), ("pos_shift", _P), ("pos_per_channel", C.c_int),
         ("transpose_T", _I64), ("headmajor_T", _I64), ("headmajor_B", _I64),
         ("out_rowsum", _P), ("tile_n", C.c_int), ("gelu_table", _P),
+        ("vt_out", _P), ("vt_ld", _I64), ("vt_col0", _I64), ("vt_T", _I64),
     ]
 
 
@@ -89,7 +90,7 @@ class AttnDesc(C.Structure):
         ("Tk_dev", _P), ("Tk_cap", _I64), ("mask_mode", C.c_int), ("mask", _P),
         ("qk_multiplier", _U8), ("qk_shift", _I8), ("frac_bits", _I32),
         ("av_multiplier", _U8), ("av_shift", _I8), ("rsqrt_offset", _I32),
-        ("exp_table", _P), ("vt", _P), ("vt_ld", _I64),
+        ("exp_table", _P), ("vt", _P), ("vt_ld", _I64), ("vt_ready", C.c_int),
     ]
 
 

@@ -473,15 +473,22 @@ __global__ void transpose_v_kernel(const int8_t *__restrict__ v, int64_t ldv, in
     }
 }
 
-cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld,
+cudaError_t transpose_v(const int8_t *v, int64_t ldv, int B, int T, int H, int8_t *vt, int vt_ld, cudaStream_t st) {
+    if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
+    dim3 tg((vt_ld + 63) / 64, B * H);
+    transpose_v_kernel<<<tg, 256, 0, st>>>(v, ldv, B, T, H, vt, vt_ld);
+    return cudaGetLastError();
+}
+
+cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld, bool vt_ready,
                          cudaStream_t st) {
     using namespace attn;
     const int T = a.Tk;
-    // V^T
-    dim3 tg((vt_ld + 63) / 64, B * H);
-    transpose_v_kernel<<<tg, 256, 0, st>>>(a.v, a.ldv, B, T, H, vt, vt_ld);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
+    if (!vt_ready) {
+        e = transpose_v(a.v, a.ldv, B, T, H, vt, vt_ld, st);
+        if (e != cudaSuccess) return e;
+    }
     CUtensorMap tq, tk, tv;
     e = make_tmap_2d_u8(&tq, a.q, (uint64_t)H * 64, (uint64_t)B * T, (uint64_t)a.ldq, 64, BQ, CU_TENSOR_MAP_SWIZZLE_64B);
     if (e != cudaSuccess) return e;

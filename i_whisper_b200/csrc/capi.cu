@@ -372,6 +372,14 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     if (d->headmajor_T && (d->N % 64 || d->headmajor_B <= 0 || d->M != d->headmajor_B * d->headmajor_T))
         return fail(IW_EINVAL, "iw_gemm_i8: head-major layout needs N%%64==0 and M == B*T");
     if (d->transpose_T && d->M % d->transpose_T) return fail(IW_EINVAL, "iw_gemm_i8: M must be a multiple of T");
+    if (d->vt_out) {
+        if (d->mode != IW_GEMM_INT8 || d->headmajor_T || d->transpose_T || d->pos || d->gelu_table)
+            return fail(IW_EINVAL, "iw_gemm_i8: vt_out applies to plain int8 row-major outputs");
+        if (d->vt_T <= 0 || d->M % d->vt_T || d->vt_col0 < 0 || d->vt_col0 % 64 || d->vt_col0 >= d->N ||
+            (d->N - d->vt_col0) % 64 || d->vt_ld < d->vt_T || d->vt_ld % 16 ||
+            (reinterpret_cast<uintptr_t>(d->vt_out) & 15))
+            return fail(IW_EINVAL, "iw_gemm_i8: invalid vt_out layout");
+    }
     iw::EpiParams p;
     p.out = d->out;
     p.ldo = d->ldo;
@@ -413,6 +421,23 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     p.hm_B = (int)d->headmajor_B;
     p.rowsum_out = d->out_rowsum;
     p.gelu_tab = d->gelu_table;
+    if (d->vt_out && !iw::cm_enabled()) {
+        // row-major kernel: all channels row-major, then V^T by a transpose
+        iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
+        if (int r = cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8"))
+            return r;
+        const int Tv = (int)d->vt_T, Bv = (int)(d->M / d->vt_T), Hv = (int)((d->N - d->vt_col0) / 64);
+        return cuda_check(iw::transpose_v(reinterpret_cast<const int8_t *>(d->out) + d->vt_col0, d->ldo, Bv, Tv, Hv,
+                                          d->vt_out, (int)d->vt_ld, S(stream)),
+                          "iw_gemm_i8");
+    }
+    if (d->vt_out) {
+        p.tr_out = d->vt_out;
+        p.tr_c0 = (int)d->vt_col0;
+        p.tr_N = (int)(d->N - d->vt_col0);
+        p.tr_T = (int)d->vt_T;
+        p.tr_ld = d->vt_ld;
+    }
     if (d->gelu_table && (d->lut || d->mode != IW_GEMM_INT8 || !d->multiplier))
         return fail(IW_EINVAL, "iw_gemm_i8: gelu_table needs a per-channel int8 epilogue without lut");
     iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
@@ -456,7 +481,8 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream) {
                     d->y_bs == d->Tq * d->ldy && (d->ldy % 16) == 0 && (reinterpret_cast<uintptr_t>(d->y) & 15) == 0 &&
                     d->vt_ld >= d->Tk && (d->vt_ld % 16) == 0 && (reinterpret_cast<uintptr_t>(d->vt) & 15) == 0;
     if (tc)
-        return cuda_check(iw::attention_tc(a, (int)d->B, (int)d->H, d->exp_table, d->vt, (int)d->vt_ld, S(stream)),
+        return cuda_check(iw::attention_tc(a, (int)d->B, (int)d->H, d->exp_table, d->vt, (int)d->vt_ld,
+                                           d->vt_ready != 0, S(stream)),
                           "iw_attention_ex");
     return cuda_check(iw::attention_cc(a, (int)d->B, (int)d->H, S(stream)), "iw_attention_ex");
 }

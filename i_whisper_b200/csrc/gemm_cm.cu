@@ -1,0 +1,546 @@
+// gemm_cm.cu -- channel-major variant of the persistent tcgen05 (kind::i8)
+// GEMM: the weight tile is the MMA's 128-row operand and BR activation rows
+// are its N operand, so TMEM lane i of the accumulator holds output channel
+// n0 + i and column j holds row m0 + j.
+//
+// Why: the I-Whisper epilogues are per-output-channel (bias, weight zero
+// point, u32 multiplier, shift, GeLU parameters). With one channel per
+// epilogue thread those constants live in registers for the whole tile; the
+// only per-row value, the zero-point row sum of X, is broadcast from shared
+// memory once per four elements. The row-major kernel (gemm_i8.cu) instead
+// re-reads two 16-byte column records from shared memory per element, and
+// shared-memory bandwidth is what the tensor pipe also feeds on.
+//
+// Work split per CTA (one CTA per SM, persistent over tiles):
+//   warp 0      : TMA producer: per 128-deep k-block a 128x128 W tile and a
+//                 BRx128 X tile (128-byte swizzle, K-major) into a ring.
+//   warp 1      : TMEM allocation (2*BR columns) and the single-thread
+//                 tcgen05.mma 128xBRx32 issue loop, committing stages and
+//                 accumulator buffers.
+//   warps 2..9  : epilogue; warp w reads TMEM lane quadrant w%4 (32
+//                 channels) and every other 32-row chunk.
+// Outputs: int8 row-major, int8 head-major (K/V caches), int8 transposed per
+// batch (V^T for the attention's P.V operand, or [B, N, T]), int16 after
+// Residual15, int16 after the positional add-requant; optional per-row sums
+// of the int8 output for the next GEMM's zero point. All waits are bounded.
+#include "gemm_i8.cuh"
+#include "iw_common.cuh"
+#include "iw_sm100.cuh"
+#include "iw_tmap.cuh"
+
+namespace iw {
+
+template <int BR, bool GT>
+struct CmCfg {
+    static constexpr int A_BYTES = 128 * kBlockK;  // W tile
+    static constexpr int B_BYTES = BR * kBlockK;   // X tile
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RS_BYTES = BR * 4;        // row sums of the tile's rows
+    static constexpr int PART_BYTES = 4 * BR * 4;  // per-quadrant partial output row sums
+    static constexpr int GTAB_BYTES = GT ? 128 * 256 : 0;  // the tile's GeLU table, lane-interleaved
+    static constexpr int FIXED = 1024 + 256 + RS_BYTES + PART_BYTES + GTAB_BYTES;
+    static constexpr int STAGES_FIT = (232448 - FIXED) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static constexpr int TMEM_COLS = 2 * BR;
+    static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
+    static_assert(STAGES >= 3, "shared memory too small");
+};
+
+// rounding_rshift(x, s) (fixedpoint.h:47-87) with the shift folded into
+// constants: s == 0 -> x, s >= 32 -> 0, otherwise
+// (int32)((u32)x + 2^(s-1) - (x < 0)) >> s.
+struct RrsK {
+    int32_t rnd, sgn, sh, z;
+};
+IW_DEV RrsK rrs_k(uint32_t s) {
+    if (s == 0) return {0, 0, 0, -1};
+    if (s < 32) return {(int32_t)(1u << (s - 1)), -1, (int32_t)s, -1};
+    return {0, 0, 0, 0};
+}
+IW_DEV int32_t rrs_apply(int32_t x, const RrsK &k) {
+    const int32_t t = u_add(u_add(x, k.rnd), (x >> 31) & k.sgn);
+    return (t >> k.sh) & k.z;
+}
+
+// Everything the epilogue needs about its channel, loaded once per tile.
+struct ChanK {
+    int32_t bias, nwz, mul, hmask;  // acc + bias - wz*rowsum; mulh by u32 multiplier
+    RrsK q;                          // Linear8: rrs shift; Linear32: {sh, z} of the left shift
+    int32_t gmi, gmo;                // GeLU multipliers (gelu_scalar.cpp)
+    RrsK gi, go;                     // GeLU shifts (clamped to [0, 32])
+    int32_t pm;                      // positional add-requant multiplier
+    RrsK ps;
+};
+
+IW_DEV ChanK load_chan(const EpiParams &p, int n, bool cv, int mode) {
+    ChanK c{};
+    c.q = {0, 0, 0, 0};
+    c.gi = c.go = c.ps = {0, 0, 0, 0};
+    if (!cv) return c;
+    uint32_t m, sh;
+    if (p.per_channel) {
+        m = __ldg(p.mult + n);
+        sh = (uint32_t)(int32_t)__ldg(p.shift + n);
+    } else {
+        m = p.smult;
+        sh = p.sshift;
+    }
+    c.bias = p.bias ? __ldg(p.bias + n) : 0;
+    c.nwz = p.wz ? -(int32_t)__ldg(p.wz + n) : 0;
+    c.mul = (int32_t)m;
+    c.hmask = (m >> 31) ? -1 : 0;
+    if (mode == EPI_L8) {
+        c.q = rrs_k(sh);
+    } else {  // Linear32: wrapping left shift, 0 for shifts >= 32 (linear32_simd.cpp:231-255)
+        c.q = sh < 32 ? RrsK{0, 0, (int32_t)sh, -1} : RrsK{0, 0, 0, 0};
+    }
+    if (p.gelu) {
+        const int ci = p.gelu_in_pc ? n : 0, co = p.gelu_out_pc ? n : 0;
+        c.gmi = __ldg(p.gmi + ci);
+        c.gmo = __ldg(p.gmo + co);
+        c.gi = rrs_k((uint32_t)clampi(__ldg(p.gsi + ci), 0, 32));
+        c.go = rrs_k((uint32_t)clampi(__ldg(p.gso + co), 0, 32));
+    }
+    if (p.posadd) {
+        const int pi = p.pos_pc ? n : 0;
+        c.pm = (int32_t)__ldg(p.pm + pi);
+        const int32_t s = __ldg(p.ps + pi);
+        c.ps = rrs_k((uint32_t)(s > 0 ? s : 0));
+    }
+    return c;
+}
+
+// gelu_scalar.cpp:10-181 for one int8 value with the 16-entry LUT held in
+// four registers.
+IW_DEV int32_t gelu_k(int32_t x, const ChanK &c, const uint32_t (&lut)[4]) {
+    int32_t i = rrs_apply(x * c.gmi, c.gi);
+    i = clampi(i + 8, 0, 15);
+    const uint32_t sel = (uint32_t)i & 7u;
+    const uint32_t lo = __byte_perm(lut[0], lut[1], sel), hi = __byte_perm(lut[2], lut[3], sel);
+    const int32_t l = (int32_t)(((i & 8) ? hi : lo) & 0xFFu);
+    const int32_t v = rrs_apply(x * l * c.gmo, c.go);
+    return clampi(v, -127, 127);
+}
+
+// GeLU through the tile's table in shared memory. The table of channel
+// (quadrant q, lane l) holds its 256 results with byte t (value t - 128) in
+// word q*2048 + (t/4)*32 + l, so the 32 lanes of a warp, whatever values
+// they look up, read 32 different banks. gw points at word q*2048 + 32*32 + l
+// (the +32 rows absorb the +128 offset of the value).
+IW_DEV int32_t gelu_tab_k(int32_t x, const uint32_t *gw) {
+    const uint32_t w = gw[(x >> 2) * 32];
+    const uint32_t b = (uint32_t)x & 3u;
+    return (int32_t)(int8_t)(uint8_t)(w >> (b << 3));  // byte b, sign-extended
+}
+
+template <int BR, int MODE, bool GT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_cm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N,
+                   int K, const EpiParams p) {
+    using Cfg = CmCfg<BR, GT>;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * Cfg::A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile uint32_t *abort_flag = tmem_slot + 1;
+    volatile uint32_t *stop_s = tmem_slot + 2;
+    int32_t *rs_s = reinterpret_cast<int32_t *>(smem + S * Cfg::STAGE_BYTES + 256);
+    int32_t *part = rs_s + BR;
+    uint32_t *gtab_s = reinterpret_cast<uint32_t *>(part + 4 * BR);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int ch_tiles = (N + 127) / 128;
+    const int row_tiles = (M + BR - 1) / BR;
+    const int tiles = ch_tiles * row_tiles;
+    const int kblocks = (K + kBlockK - 1) / kBlockK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *stop_s = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmW);
+        prefetch_tmap(&tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, last_parity = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+                const int m0 = (tile / ch_tiles) * BR;
+                const int n0 = (tile % ch_tiles) * 128;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
+                    mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+                    tma_load_2d(&tmW, &full[stage], sA + stage * Cfg::A_BYTES, kb * kBlockK, n0);
+                    tma_load_2d(&tmX, &full[stage], sB + stage * Cfg::B_BYTES, kb * kBlockK, m0);
+                    issued_mask |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) { stage = 0; phase ^= 1; }
+                }
+            }
+            // every copy this thread issued must land before the CTA exits
+            for (int s = 0; s < S; ++s)
+                if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(128, BR);
+            int stage = 0;
+            uint32_t phase = 0;
+            int buf = 0;
+            uint32_t bphase = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[buf], bphase ^ 1)) { *abort_flag = 1; break; }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BR);
+                bool ok = true;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * Cfg::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+                    for (int ks = 0; ks < kBlockK / 32; ++ks)
+                        mma_i8(d, sdesc_kmajor_sw128(a0 + ks * 32), sdesc_kmajor_sw128(b0 + ks * 32), idesc,
+                               (kb | ks) != 0);
+                    mma_commit(&empty[stage]);
+                    if (++stage == S) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) { *abort_flag = 1; break; }
+                mma_commit(&tfull[buf]);
+                buf ^= 1;
+                if (buf == 0) bphase ^= 1;
+            }
+            mma_commit(drain);
+            mbar_wait(drain, 0);
+        }
+    } else {
+        const int ew = warp - 2;
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may read
+        const int slice = ew >> 2;  // 0: even 32-row chunks, 1: odd ones
+        const int et = ew * 32 + lane;
+        uint32_t lut[4] = {0, 0, 0, 0};
+        if (p.gelu) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+                lut[w] = (uint32_t)p.lut[4 * w] | ((uint32_t)p.lut[4 * w + 1] << 8) |
+                         ((uint32_t)p.lut[4 * w + 2] << 16) | ((uint32_t)p.lut[4 * w + 3] << 24);
+        }
+        int buf = 0;
+        uint32_t bphase = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            const int m0 = (tile / ch_tiles) * BR;
+            const int n0 = (tile % ch_tiles) * 128;
+            // Barrier A: every epilogue warp is done with the previous tile's
+            // shared row sums and partials. One thread samples the abort flag
+            // so that all epilogue warps take the same decision.
+            epi_bar();
+            if (et == 0) *stop_s = *abort_flag;
+            for (int i = et; i < BR; i += kEpiWarps * 32)
+                rs_s[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
+            if constexpr (GT) {
+                // 16 table bytes of one channel per thread; a warp covers 32
+                // consecutive channels, so the four word stores hit 32 banks
+                for (int i = et; i < 128 * 16; i += kEpiWarps * 32) {
+                    const int ch = i & 127, tq = i >> 7;
+                    int4 t4 = make_int4(0, 0, 0, 0);
+                    if (n0 + ch < N) t4 = __ldg(reinterpret_cast<const int4 *>(p.gelu_tab + (int64_t)(n0 + ch) * 256) + tq);
+                    uint32_t *dst = gtab_s + (ch >> 5) * 2048 + tq * 4 * 32 + (ch & 31);
+                    dst[0] = (uint32_t)t4.x;
+                    dst[32] = (uint32_t)t4.y;
+                    dst[64] = (uint32_t)t4.z;
+                    dst[96] = (uint32_t)t4.w;
+                }
+            }
+            epi_bar();
+            if (*stop_s) break;
+
+            const int n = n0 + quad * 32 + lane;
+            const bool cv = n < N;
+            const ChanK ck = load_chan(p, n, cv, MODE);
+            const bool to_tr = p.tr_out && n >= p.tr_c0;
+            // Checkpoints made by the quantiser's frexp rule have multipliers
+            // below 2^31 and shifts in [1, 31]; for such a warp the MULH needs
+            // no correction and the rounding shift is three instructions.
+            const bool simple = MODE == EPI_L8 && __all_sync(0xffffffffu, !cv || (ck.hmask == 0 && ck.q.sgn == -1));
+
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&tfull[buf], bphase);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) {
+                if (lane == 0) *abort_flag = 1;
+            } else {
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = slice; c < BR / 32; c += 2) {
+                    const int r0 = m0 + c * 32;
+                    if (r0 >= M) break;  // warp-uniform
+                    uint32_t acc[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BR + c * 32),
+                                       acc);
+                    tmem_ld_wait();
+                    const int4 *rs4 = reinterpret_cast<const int4 *>(rs_s + c * 32);
+                    int32_t v[32];
+                    if (simple) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const int4 r4 = rs4[q];
+                            const int32_t rs[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = 4 * q + u;
+                                const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                const int32_t h = __mulhi(a, ck.mul);
+                                v[j] = clampi(u_add(u_add(h, ck.q.rnd), h >> 31) >> ck.q.sh, -127, 127);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const int4 r4 = rs4[q];
+                            const int32_t rs[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int j = 4 * q + u;
+                                const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                const int32_t h = u_add(__mulhi(a, ck.mul), a & ck.hmask);
+                                if constexpr (MODE == EPI_L8) {
+                                    v[j] = clampi(rrs_apply(h, ck.q), -127, 127);
+                                } else {
+                                    v[j] = (int32_t)((uint32_t)h << ck.q.sh) & ck.q.z;
+                                }
+                            }
+                        }
+                    }
+                    if constexpr (MODE == EPI_L32_RES) {
+                        // residual15_scalar.cpp:9-27 on the Linear32 output
+                        if (cv) {
+                            const int rm = (int32_t)p.res_mult;
+                            int16_t *out = reinterpret_cast<int16_t *>(p.out);
+                            // The residual is usually updated in place (res == out):
+                            // load the chunk's 32 residuals before the first store so
+                            // the loads overlap instead of waiting on each store.
+                            int32_t rv[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                rv[j] = (r0 + j < M) ? (int32_t)p.res[(int64_t)(r0 + j) * p.ldr + n] : 0;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const int64_t m = r0 + j;
+                                if (m < M) {
+                                    int32_t t = u_mad(rv[j], rm, v[j]);
+                                    t = u_add(u_add(t, 1 << 14), t >> 31) >> 15;
+                                    out[m * p.ldo + n] = (int16_t)clampi(t, -16383, 16383);
+                                }
+                            }
+                        }
+                    } else {
+                        if constexpr (GT) {
+                            const uint32_t *gw = gtab_s + quad * 2048 + 32 * 32 + lane;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = gelu_tab_k(v[j], gw);
+                        } else if (p.gelu) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = gelu_k(v[j], ck, lut);
+                        }
+                        if (!cv) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = 0;
+                        }
+                        if (p.posadd) {
+                            // add_requant15_scalar.cpp:29-80, int16 result
+                            if (cv) {
+                                int16_t *out = reinterpret_cast<int16_t *>(p.out);
+                                int32_t pe[32];
+                                int t = r0 % p.pe_T;
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    pe[j] = (r0 + j < M) ? (int32_t)__ldg(p.pe + (int64_t)t * N + n) : 0;
+                                    if (++t == p.pe_T) t = 0;
+                                }
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    if (r0 + j < M) {
+                                        const int32_t a = clampi(rrs_apply(wmul(v[j] + pe[j], ck.pm), ck.ps), -16383, 16383);
+                                        out[(int64_t)(r0 + j) * p.ldo + n] = (int16_t)a;
+                                    }
+                                }
+                            }
+                        } else if (to_tr) {
+                            // per-batch transposed rows: tr_out[(b*tr_N + n - tr_c0)*tr_ld + t]
+                            if (cv) {
+                                int b = r0 / p.tr_T, t = r0 - (r0 / p.tr_T) * p.tr_T;
+                                const bool vec = (p.tr_T & 3) == 0 && (p.tr_ld & 3) == 0 &&
+                                                 (reinterpret_cast<uintptr_t>(p.tr_out) & 3) == 0;
+#pragma unroll
+                                for (int j = 0; j < 32; j += 4) {
+                                    const int m = r0 + j;
+                                    if (vec && m + 3 < M) {
+                                        int8_t *dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
+                                        *reinterpret_cast<uint32_t *>(dst) =
+                                            (uint32_t)(uint8_t)v[j] | ((uint32_t)(uint8_t)v[j + 1] << 8) |
+                                            ((uint32_t)(uint8_t)v[j + 2] << 16) | ((uint32_t)(uint8_t)v[j + 3] << 24);
+                                        t += 4;
+                                        if (t == p.tr_T) { t = 0; ++b; }
+                                    } else {
+#pragma unroll
+                                        for (int u = 0; u < 4; ++u) {
+                                            if (m + u < M)
+                                                p.tr_out[((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t] =
+                                                    (int8_t)v[j + u];
+                                            if (++t == p.tr_T) { t = 0; ++b; }
+                                        }
+                                    }
+                                }
+                            }
+                        } else if (p.hm_T) {
+                            // head-major K/V cache rows
+                            if (cv) {
+                                int8_t *base = reinterpret_cast<int8_t *>(p.out) + (int64_t)(n >> 6) * p.hm_B * p.hm_T * 64 +
+                                               (n & 63);
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (r0 + j < M) base[(int64_t)(r0 + j) * 64] = (int8_t)v[j];
+                            }
+                        } else if (cv) {
+                            int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
+                            if (r0 + 32 <= M) {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    *out = (int8_t)v[j];
+                                    out += p.ldo;
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    if (r0 + j < M) *out = (int8_t)v[j];
+                                    out += p.ldo;
+                                }
+                            }
+                        }
+                        if (p.rowsum_out) {
+                            // per row, the sum over this warp's 32 channels
+                            int32_t rsum[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) rsum[j] = __reduce_add_sync(0xffffffffu, v[j]);
+                            if (lane == 0) {
+                                int4 *dst = reinterpret_cast<int4 *>(part + quad * BR + c * 32);
+#pragma unroll
+                                for (int q4 = 0; q4 < 8; ++q4)
+                                    dst[q4] = make_int4(rsum[4 * q4], rsum[4 * q4 + 1], rsum[4 * q4 + 2], rsum[4 * q4 + 3]);
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            buf ^= 1;
+            if (buf == 0) bphase ^= 1;
+            if (MODE == EPI_L8 && p.rowsum_out) {
+                // Barrier C: all four quadrants' partial sums of each row are in.
+                epi_bar();
+                for (int i = et; i < BR; i += kEpiWarps * 32)
+                    if (m0 + i < M)
+                        atomicAdd(p.rowsum_out + m0 + i, part[i] + part[BR + i] + part[2 * BR + i] + part[3 * BR + i]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+template <int BR, int MODE, bool GT>
+static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStream_t stream) {
+    using Cfg = CmCfg<BR, GT>;
+    CUtensorMap tw, tx;
+    cudaError_t e = make_tmap_2d_u8(&tw, g.w, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.ldw, kBlockK, 128);
+    if (e != cudaSuccess) return e;
+    e = make_tmap_2d_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, BR);
+    if (e != cudaSuccess) return e;
+    static bool attr_set = false;
+    if (!attr_set) {
+        e = cudaFuncSetAttribute(gemm_cm_kernel<BR, MODE, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const long tiles = (long)((g.N + 127) / 128) * ((g.M + BR - 1) / BR);
+    const int grid = tiles < num_sms() ? (int)tiles : num_sms();
+    gemm_cm_kernel<BR, MODE, GT><<<grid, kThreads, Cfg::SMEM, stream>>>(tw, tx, g.M, g.N, g.K, p);
+    return cudaGetLastError();
+}
+
+template <int MODE, bool GT>
+static cudaError_t launch_cm_mode(const GemmShape &g, const EpiParams &p, cudaStream_t stream, int br) {
+    if (br == 64) return launch_cm_t<64, MODE, GT>(g, p, stream);
+    if (br == 128) return launch_cm_t<128, MODE, GT>(g, p, stream);
+    return launch_cm_t<256, MODE, GT>(g, p, stream);
+}
+
+// The channel-major path covers Linear8 (per-channel or scalar requant,
+// optional GeLU from its parameters, positional add, row-major, head-major
+// or per-batch transposed int8 output, optional output row sums) and
+// Linear32 + Residual15. GeLU lookup tables are a row-major-path feature.
+bool cm_eligible(const GemmShape &g, EpiMode mode, const EpiParams &p) {
+    // Linear32 + Residual15 stays on the row-major kernel, which reads and
+    // writes the INT15 residual rows with 16-byte accesses and measured
+    // faster (2141 vs 2083 TOPS at K=4096, 790 vs 600 at K=1024).
+    if (mode != EPI_L8) return false;
+    if (p.vt_T) return false;
+    if (p.gelu_tab && (p.gelu || !p.per_channel || p.posadd)) return false;
+    if (mode == EPI_L32_RES && (!p.per_channel || p.gelu || p.posadd || p.hm_T || p.tr_out || p.rowsum_out))
+        return false;
+    if (mode == EPI_L32_RES && (reinterpret_cast<uintptr_t>(p.out) & 1)) return false;
+    if (p.posadd && (p.hm_T || p.tr_out || p.rowsum_out)) return false;
+    if (p.tr_out && (p.tr_T <= 0 || p.tr_N <= 0)) return false;
+    return true;
+}
+
+cudaError_t gemm_cm_launch(const GemmShape &g, EpiMode mode, const EpiParams &p, cudaStream_t stream, int br) {
+    if (br == 0) {
+        const long ch_tiles = (g.N + 127) / 128;
+        br = 256;
+        if (ch_tiles * ((g.M + 255) / 256) < num_sms() / 2) br = 128;
+        if (ch_tiles * ((g.M + 127) / 128) < num_sms() / 2) br = 64;
+    }
+    if (mode == EPI_L8) {
+        if (p.gelu_tab) return launch_cm_mode<EPI_L8, true>(g, p, stream, br);
+        return launch_cm_mode<EPI_L8, false>(g, p, stream, br);
+    }
+    return launch_cm_mode<EPI_L32_RES, false>(g, p, stream, br);
+}
+
+}  // namespace iw

@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_i8.cuh"
@@ -526,6 +527,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+bool cm_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("IW_GEMM_ROWMAJOR");
+        on = (e && e[0] == '1') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 int num_sms() {
     static int n = 0;
     if (n == 0) {
@@ -583,6 +593,20 @@ cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p,
     if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaErrorInvalidValue;
     if ((g.ldx % 16) != 0 || (g.ldw % 16) != 0 || (g.K % 16) != 0) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(g.x) & 15) || (reinterpret_cast<uintptr_t>(g.w) & 15)) return cudaErrorMisalignedAddress;
+    if (cm_enabled()) {
+        EpiParams q = p;
+        if (q.transpose_T && !q.tr_out) {
+            q.tr_out = reinterpret_cast<int8_t *>(q.out);
+            q.tr_c0 = 0;
+            q.tr_N = g.N;
+            q.tr_T = q.transpose_T;
+            q.tr_ld = q.transpose_T;
+            q.transpose_T = 0;
+        }
+        if (cm_eligible(g, mode, q))
+            return gemm_cm_launch(g, mode, q, stream, (bn_hint == 64 || bn_hint == 128 || bn_hint == 256) ? bn_hint : 0);
+    }
+    if (p.tr_out) return cudaErrorInvalidValue;  // transposed outputs need the channel-major kernel
     int bn = bn_hint;
     if (bn == 0) {
         // Prefer wide tiles; fall back to narrower ones when the grid would

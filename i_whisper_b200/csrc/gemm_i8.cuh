@@ -65,6 +65,12 @@ struct EpiParams {
     // indexed by (requantised value + 128); built by gelu_table_build from
     // the same GeLU parameters, so it is exact
     const int8_t *gelu_tab = nullptr;
+    // optional (channel-major path): int8 results of channels n >= tr_c0
+    // are written per batch transposed, tr_out[(b*tr_N + n - tr_c0)*tr_ld + t]
+    // with m = b*tr_T + t, instead of row-major (V^T for the attention)
+    int8_t *tr_out = nullptr;
+    int tr_c0 = 0, tr_N = 0, tr_T = 0;
+    int64_t tr_ld = 0;
 };
 
 // Builds tab[n][x+128] = GeLU_n(x) for x in [-128, 127] (gelu_scalar.cpp).
@@ -83,6 +89,14 @@ struct GemmShape {
 // Returns a cudaError_t (cudaSuccess when the launch was queued).
 cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p, cudaStream_t stream,
                            int bn_hint = 0);
+
+// Channel-major kernel (gemm_cm.cu): the weight tile is the MMA's 128-row
+// operand, so each epilogue thread owns one output channel.
+bool cm_eligible(const GemmShape &g, EpiMode mode, const EpiParams &p);
+cudaError_t gemm_cm_launch(const GemmShape &g, EpiMode mode, const EpiParams &p, cudaStream_t stream, int br);
+// False when IW_GEMM_ROWMAJOR=1 is set in the environment (selects the
+// row-major kernel for every GEMM; used to compare the two).
+bool cm_enabled();
 
 // Number of SMs of the current device (cached).
 int num_sms();

@@ -69,7 +69,11 @@ cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st);
 // Q/K rows straight from the projection buffer (16-byte aligned, batch
 // stride T*ld, head h at column h*64), V transposed into vt [B*H*64, vt_ld]
 // (vt_ld >= T, multiple of 16). tab from shift_exp_table_build.
-cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld, cudaStream_t st);
+// vt_ready: vt already holds V^T (written by the QKV GEMM), skip the transpose.
+cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld, bool vt_ready,
+                         cudaStream_t st);
+// V^T of head-major V columns: vt[(b*H + h)*64 + d][t] = v[(b*T + t)*ldv + h*64 + d].
+cudaError_t transpose_v(const int8_t *v, int64_t ldv, int B, int T, int H, int8_t *vt, int vt_ld, cudaStream_t st);
 // Builds the shift-exp table for frac_bits fb into tab (>= 32772 bytes);
 // scratch2 is two device ints, scratch2[1] == 1 afterwards when the table is
 // too long for the tensor-core kernel.

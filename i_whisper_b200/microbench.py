@@ -67,7 +67,8 @@ def _gauss_i8(g: torch.Generator, *shape) -> torch.Tensor:
     return torch.clamp(torch.round(torch.randn(shape, generator=g) * 30.0), -127, 127).to(torch.int8).cuda()
 
 
-def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: int) -> dict:
+def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: int, gelu: str = "none",
+               rowsum_out: bool = False) -> dict:
     g = torch.Generator().manual_seed(seed)
     x, w = _i8(g, M, K), _i8(g, N, K)
     rng = np.random.default_rng(seed)
@@ -89,6 +90,24 @@ def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: 
         out = torch.empty(M, N, dtype=torch.int8, device="cuda")
         d.mode = _lib.IW_GEMM_INT8
         out_bytes = M * N
+        if gelu != "none":  # fc1 form: per-channel GeLU on the int8 result
+            gp = [torch.from_numpy(a).cuda() for a in (
+                rng.integers(0, 256, 16).astype(np.uint8), rng.integers(0, 256, N).astype(np.uint8),
+                rng.integers(0, 12, N).astype(np.int8), rng.integers(0, 256, N).astype(np.uint8),
+                rng.integers(6, 14, N).astype(np.int8))]
+            keep += gp
+            if gelu == "table":
+                tab = torch.empty(N, 256, dtype=torch.int8, device="cuda")
+                keep.append(tab)
+                _lib.call("iw_gelu_table", *[t.data_ptr() for t in gp], N, N, N, tab.data_ptr(), stream)
+                d.gelu_table = tab.data_ptr()
+            else:
+                d.lut, d.luti_multiplier, d.luti_shift, d.luto_multiplier, d.luto_shift = [t.data_ptr() for t in gp]
+                d.luti_per_channel = d.luto_per_channel = 1
+        if rowsum_out:
+            rso = torch.zeros(M, dtype=torch.int32, device="cuda")
+            keep.append(rso)
+            d.out_rowsum = rso.data_ptr()
     else:  # linear32 + residual15 (out-projection / fc2)
         out = torch.empty(M, N, dtype=torch.int16, device="cuda")
         res = torch.randint(-16383, 16384, (M, N), dtype=torch.int16, generator=g).cuda()
@@ -99,7 +118,8 @@ def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: 
     d.out, d.ldo = out.data_ptr(), N
     ms = _time(lambda: _lib.check(_lib.LIB.iw_gemm_i8(C.byref(d), stream)), reps)
     tops = 2.0 * M * N * K / ms / 1e9
-    return {"op": "gemm", "mode": mode, "M": M, "K": K, "N": N, "tile_n": tile_n, "ms": round(ms, 4),
+    return {"op": "gemm", "mode": mode, "gelu": gelu, "rowsum_out": rowsum_out, "M": M, "K": K, "N": N,
+            "tile_n": tile_n, "ms": round(ms, 4),
             "tops": round(tops, 1), "frac_of_datasheet_4500": round(tops / DATASHEET_INT8_TOPS, 4),
             "algorithmic_bytes": M * K + N * K + out_bytes}
 
@@ -181,6 +201,9 @@ def main(argv=None):
     p.add_argument("--N", type=int, default=4096)
     p.add_argument("--mode", choices=["linear8", "linear32_residual15"], default="linear8")
     p.add_argument("--tile-n", type=int, default=0, help="GEMM N tile (0: library choice)")
+    p.add_argument("--gelu", choices=["none", "params", "table"], default="none",
+                   help="Linear8 with per-channel GeLU from its parameters or from a lookup table")
+    p.add_argument("--rowsum-out", action="store_true", help="also accumulate the output row sums")
     p.add_argument("--rows", type=int, default=1500)
     p.add_argument("--d", type=int, default=1024)
     p.add_argument("--B", type=int, default=4)
@@ -193,7 +216,7 @@ def main(argv=None):
         raise SystemExit("microbench needs a CUDA device")
     torch.cuda.set_device(0)
     if a.op == "gemm":
-        r = bench_gemm(a.M, a.K, a.N, a.mode, a.tile_n, a.reps, a.seed)
+        r = bench_gemm(a.M, a.K, a.N, a.mode, a.tile_n, a.reps, a.seed, a.gelu, a.rowsum_out)
     elif a.op == "layernorm":
         r = bench_layernorm(a.rows, a.d, a.reps, a.seed)
     elif a.op == "attention":

@@ -222,6 +222,14 @@ typedef struct iw_gemm_desc {
      * instead of the lut and luti/luto parameters on per-channel Linear8
      * outputs */
     const int8_t *gelu_table;
+    /* optional V^T output for the tensor-core attention: int8 results of
+     * channels n >= vt_col0 go to vt_out[(b*(N-vt_col0) + n-vt_col0)*vt_ld + t]
+     * (m = b*vt_T + t) instead of out; vt_col0 a multiple of 64, M a
+     * multiple of vt_T, vt_ld >= vt_T and a multiple of 16 */
+    int8_t *vt_out;
+    int64_t vt_ld;
+    int64_t vt_col0;
+    int64_t vt_T;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */
@@ -255,6 +263,9 @@ typedef struct iw_attn_desc {
     const uint8_t *exp_table;
     int8_t *vt;
     int64_t vt_ld;
+    /* 1: vt already holds V^T (written by the projection GEMM's vt_out), so
+     * the call does not transpose V */
+    int vt_ready;
 } iw_attn_desc;
 
 int iw_attention_ex(const iw_attn_desc *d, void *stream);

@@ -321,6 +321,69 @@ def test_linear8_gelu_table_rowsum(ops, L, M, K, N):
     assert np.array_equal(host(rs_out), ref.astype(np.int32).sum(1))
 
 
+@pytest.mark.parametrize("M,K,N,pc", [(300, 1024, 4096, 1), (129, 384, 1536, 1), (7, 1280, 5120, 1),
+                                      (515, 256, 1000, 1), (64, 512, 200, 0), (1500, 384, 1536, 1)])
+def test_linear8_gelu_params_rowsum(ops, L, M, K, N, pc):
+    """fc1 form on the channel-major kernel: Linear8 -> GeLU computed from its
+    parameters (per-channel or per-tensor), with the row sums of the int8
+    output accumulated for the next GEMM's zero point."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(M + N + pc)
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=-2)
+    n_g = N if pc else 1
+    lut = rng.integers(0, 256, 16, dtype=np.uint8)
+    mi = rng.integers(0, 256, n_g, dtype=np.uint8); si = rng.integers(-2, 34, n_g).astype(np.int8)
+    mo = rng.integers(0, 256, n_g, dtype=np.uint8); so = rng.integers(-2, 34, n_g).astype(np.int8)
+    ref = L.gelu(L.linear8(x, w, b, wz, m, s), lut, mi, si, mo, so)
+    X, W = dev(x), dev(w)
+    st = torch.cuda.current_stream().cuda_stream
+    gp = [dev(a) for a in (lut, mi, si, mo, so)]
+    rs = torch.from_numpy(x.astype(np.int32).sum(1).astype(np.int32)).cuda()
+    out = torch.empty(M, N, dtype=torch.int8, device="cuda")
+    rs_out = torch.zeros(M, dtype=torch.int32, device="cuda")
+    B_, Z, Mu, S_ = dev(b), dev(wz), dev(m), dev(s)
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    d.mode, d.out, d.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
+    d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    d.lut, d.luti_multiplier, d.luti_shift, d.luto_multiplier, d.luto_shift = [t.data_ptr() for t in gp]
+    d.luti_per_channel = d.luto_per_channel = pc
+    d.out_rowsum = rs_out.data_ptr()
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
+    assert np.array_equal(host(out), ref)
+    assert np.array_equal(host(rs_out), ref.astype(np.int32).sum(1))
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 1500, 16), (3, 37, 6), (1, 1500, 20), (2, 130, 8)])
+def test_linear8_qkv_vt_out(ops, L, B, T, H):
+    """Fused QKV form: Q and K row-major, V written as V^T [B*H*64, vt_ld]
+    for the tensor-core attention by the same GEMM."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(B * T + H)
+    d_ = H * 64
+    K, N, M = d_, 3 * d_, B * T
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N)
+    ref = L.linear8(x, w, b, wz, m, s)
+    X, W = dev(x), dev(w)
+    rs = torch.from_numpy(x.astype(np.int32).sum(1).astype(np.int32)).cuda()
+    out = torch.zeros(M, N, dtype=torch.int8, device="cuda")
+    vt_ld = (T + 15) // 16 * 16
+    vt = torch.zeros(B * H * 64, vt_ld, dtype=torch.int8, device="cuda")
+    B_, Z, Mu, S_ = dev(b), dev(wz), dev(m), dev(s)
+    g = _lib.GemmDesc()
+    g.x, g.ldx, g.w, g.ldw, g.M, g.N, g.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    g.mode, g.out, g.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
+    g.bias, g.weight_zero, g.x_rowsum, g.multiplier, g.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    g.vt_out, g.vt_ld, g.vt_col0, g.vt_T = vt.data_ptr(), vt_ld, 2 * d_, T
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(g), torch.cuda.current_stream().cuda_stream))
+    got = host(out)
+    assert np.array_equal(got[:, :2 * d_], ref[:, :2 * d_])
+    want_vt = ref[:, 2 * d_:].reshape(B, T, H, 64).transpose(0, 2, 3, 1).reshape(B * H * 64, T)
+    assert np.array_equal(host(vt)[:, :T], want_vt)
+
+
 @pytest.mark.parametrize("B,T,N", [(2, 1500, 768), (3, 37, 128)])
 def test_linear8_headmajor(ops, L, B, T, N):
     """Cross-attention K/V form: Linear8 stored head-major [N/64, B, T, 64]."""
