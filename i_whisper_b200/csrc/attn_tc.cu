@@ -164,6 +164,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // TMEM is held: let the next kernel be scheduled, then wait for the
+    // previous one before touching global memory
+    pdl_launch();
+    pdl_wait();
 
     // Q and K maps cover [B*T rows, H*64 columns]; V^T maps [B*H*64, vt_ld].
     if (warp == 0) {
@@ -456,6 +460,8 @@ __global__ void shift_exp_table_fill(int32_t fb, uint8_t *tab, const int *last_n
 // (V given with row stride ldv); keys are the contiguous dimension.
 __global__ void transpose_v_kernel(const int8_t *__restrict__ v, int64_t ldv, int B, int T, int H,
                                    int8_t *__restrict__ vt, int vt_ld) {
+    pdl_wait();
+    pdl_launch();
     __shared__ int8_t tile[64][65];
     const int bh = blockIdx.y;
     const int b = bh / H, h = bh % H;
@@ -476,8 +482,7 @@ __global__ void transpose_v_kernel(const int8_t *__restrict__ v, int64_t ldv, in
 cudaError_t transpose_v(const int8_t *v, int64_t ldv, int B, int T, int H, int8_t *vt, int vt_ld, cudaStream_t st) {
     if (B <= 0 || H <= 0 || T <= 0) return cudaSuccess;
     dim3 tg((vt_ld + 63) / 64, B * H);
-    transpose_v_kernel<<<tg, 256, 0, st>>>(v, ldv, B, T, H, vt, vt_ld);
-    return cudaGetLastError();
+    return launch_pdl(transpose_v_kernel, tg, 256, 0, st, v, ldv, B, T, H, vt, vt_ld);
 }
 
 cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, int8_t *vt, int vt_ld, bool vt_ready,
@@ -521,9 +526,8 @@ cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, in
     const int items = B * H * ((T + BQ - 1) / BQ);
     const int grid = items < num_sms() ? items : num_sms();
     const bool fast = a.qk_mult >= 1 && a.qk_mult <= 255 && sh >= 1 && sh <= 31;
-    if (fast) attn_tc_kernel<true><<<grid, THREADS, SMEM, st>>>(tq, tk, tv, p);
-    else attn_tc_kernel<false><<<grid, THREADS, SMEM, st>>>(tq, tk, tv, p);
-    return cudaGetLastError();
+    if (fast) return launch_pdl(attn_tc_kernel<true>, grid, THREADS, SMEM, st, tq, tk, tv, p);
+    return launch_pdl(attn_tc_kernel<false>, grid, THREADS, SMEM, st, tq, tk, tv, p);
 }
 
 cudaError_t shift_exp_table_build(int32_t fb, uint8_t *tab, int *scratch2, cudaStream_t st) {

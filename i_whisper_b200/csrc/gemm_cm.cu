@@ -186,6 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // TMEM is held: let the next kernel be scheduled, then wait for the
+    // previous one before touching global memory
+    pdl_launch();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -499,8 +503,7 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
     }
     const long tiles = (long)((g.N + 127) / 128) * ((g.M + BR - 1) / BR);
     const int grid = tiles < num_sms() ? (int)tiles : num_sms();
-    gemm_cm_kernel<BR, MODE, GT><<<grid, kThreads, Cfg::SMEM, stream>>>(tw, tx, g.M, g.N, g.K, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_cm_kernel<BR, MODE, GT>, grid, kThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K, p);
 }
 
 template <int MODE, bool GT>

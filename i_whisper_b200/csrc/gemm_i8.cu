@@ -383,6 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // TMEM is held: let the next kernel be scheduled, then wait for the
+    // previous one before touching global memory
+    pdl_launch();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -564,8 +568,7 @@ static cudaError_t launch_t(const GemmShape &g, const EpiParams &p, cudaStream_t
     }
     const int tiles = ((g.M + kBlockM - 1) / kBlockM) * ((g.N + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    gemm_i8_kernel<BN, MODE, FLAVOR><<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, g.M, g.N, g.K, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_i8_kernel<BN, MODE, FLAVOR>, grid, kThreads, Cfg::SMEM, stream, ta, tb, g.M, g.N, g.K, p);
 }
 
 template <int MODE, int FLAVOR>

@@ -6,6 +6,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 #define IW_DEV __device__ __forceinline__
@@ -121,6 +123,15 @@ IW_DEV int32_t shift_exp_one(int32_t x, int32_t xm, int32_t fb) {
     return (int32_t)(uint8_t)e;
 }
 
+// Programmatic dependent launch. Kernels launched by launch_pdl may start
+// while the previous kernel on the stream is finishing: each kernel does its
+// private set-up (shared-memory barriers, TMEM allocation), then pdl_wait()
+// blocks until the previous grid has completed and its writes are visible,
+// before the kernel touches global memory; pdl_launch() lets the next kernel
+// be scheduled. Without the launch attribute both are no-ops.
+IW_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+IW_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Device-side status word: set by bounded waits that gave up, read by the
 // host after a synchronisation (iw_device_status in the C ABI).
 enum : uint32_t {
@@ -131,5 +142,31 @@ enum : uint32_t {
 // The library is built as one translation unit (iw_lib.cu), so this single
 // definition is shared by every kernel.
 __device__ uint32_t g_device_status = 0;
+
+// false when IW_PDL=0 is set in the environment (plain stream-ordered launches)
+inline bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("IW_PDL");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace iw

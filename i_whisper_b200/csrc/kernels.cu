@@ -15,6 +15,8 @@ namespace iw {
 // Row sums of an int8 matrix (zero-point term of Linear8/32, linear.py:89-91)
 // ---------------------------------------------------------------------------
 __global__ void rowsum_i8_kernel(const int8_t *__restrict__ x, int64_t ldx, int M, int K, int32_t *__restrict__ out) {
+    pdl_wait();
+    pdl_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
@@ -35,8 +37,7 @@ cudaError_t rowsum_i8(const int8_t *x, int64_t ldx, int M, int K, int32_t *out, 
     if (M <= 0) return cudaSuccess;
     const int threads = 256;
     const int blocks = (M * 32 + threads - 1) / threads;
-    rowsum_i8_kernel<<<blocks, threads, 0, st>>>(x, ldx, M, K, out);
-    return cudaGetLastError();
+    return launch_pdl(rowsum_i8_kernel, blocks, threads, 0, st, x, ldx, M, K, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -71,6 +72,8 @@ __global__ void __launch_bounds__(256) layernorm32_kernel(const int16_t *__restr
                                                            int8_t *__restrict__ y, int64_t ldy, int rows,
                                                            int32_t *__restrict__ rowsum_out,
                                                            int32_t *__restrict__ rowsum_zero) {
+    pdl_wait();
+    pdl_launch();
     constexpr int G = D / 128;  // groups of 4 elements per lane
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -150,11 +153,10 @@ cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, cons
         return cudaErrorMisalignedAddress;
     const int threads = 256;
     const int blocks = (rows * 32 + threads - 1) / threads;
-#define IW_LN_CASE(DD)                                                                                        \
-    case DD:                                                                                                  \
-        layernorm32_kernel<DD><<<blocks, threads, 0, st>>>(x, ldx, gamma, beta, p, y, ldy, rows, rowsum_out, \
-                                                            rowsum_zero);                                     \
-        break;
+#define IW_LN_CASE(DD)                                                                                      \
+    case DD:                                                                                                \
+        return launch_pdl(layernorm32_kernel<DD>, blocks, threads, 0, st, x, ldx, gamma, beta, p, y, ldy, rows, \
+                          rowsum_out, rowsum_zero);
     switch (d) {
         IW_LN_CASE(384)
         IW_LN_CASE(512)
@@ -164,7 +166,6 @@ cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, cons
     default: return cudaErrorInvalidValue;
     }
 #undef IW_LN_CASE
-    return cudaGetLastError();
 }
 
 // LayerNorm statistics only (layernorm32_stats_scalar): mean, variance,
@@ -289,6 +290,8 @@ __global__ void add_requant15_kernel(const int8_t *__restrict__ x, const int64_t
                                      const int8_t *__restrict__ addend, const uint16_t *__restrict__ mult,
                                      const int8_t *__restrict__ shift, int16_t *__restrict__ y, int B, int T, int C,
                                      int n_mult, int n_shift, int offset, const int32_t *offset_dev) {
+    pdl_wait();
+    pdl_launch();
     const int64_t total = (int64_t)B * T * C;
     const int off = offset_dev ? *offset_dev : offset;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -313,9 +316,8 @@ cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *
     if (total <= 0) return cudaSuccess;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 8192) blocks = 8192;
-    add_requant15_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, tokens, addend, mult, shift, y, B, T, C, n_mult, n_shift,
+    return launch_pdl(add_requant15_kernel, (unsigned)blocks, 256, 0, st, x, tokens, addend, mult, shift, y, B, T, C, n_mult, n_shift,
                                                            offset, offset_dev);
-    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -326,6 +328,8 @@ cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *
 // ---------------------------------------------------------------------------
 __global__ void im2col_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ out, int B, int Cin, int Tin, int K,
                               int stride, int pad, int Tout, int64_t ldo, int channels_last) {
+    pdl_wait();
+    pdl_launch();
     const int64_t cols = ldo;
     const int64_t total = (int64_t)B * Tout * cols;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -350,8 +354,7 @@ cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K,
     if (total <= 0) return cudaSuccess;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 16384) blocks = 16384;
-    im2col_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, out, B, Cin, Tin, K, stride, pad, Tout, ldo, channels_last);
-    return cudaGetLastError();
+    return launch_pdl(im2col_kernel, (unsigned)blocks, 256, 0, st, x, out, B, Cin, Tin, K, stride, pad, Tout, ldo, channels_last);
 }
 
 // 2-D copy into a zero-padded buffer (row stride ldo >= cols).
@@ -408,6 +411,8 @@ IW_DEV int32_t dp4a_us(uint32_t a, int32_t b, int32_t c) {
 
 template <int QB>
 __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
+    pdl_wait();
+    pdl_launch();
     extern __shared__ uint8_t smem[];
     const int Tk = a.Tk_dev ? *a.Tk_dev : a.Tk;
     const int Tq = a.Tq;
@@ -594,8 +599,7 @@ static cudaError_t attention_cc_launch(const AttnArgs &a, int B, int H, cudaStre
         smem_set = smem;
     }
     dim3 grid((a.Tq + QB - 1) / QB, H, B);
-    attn_cc_kernel<QB><<<grid, kAttnThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(attn_cc_kernel<QB>, grid, kAttnThreads, smem, st, a);
 }
 
 cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
@@ -612,6 +616,8 @@ cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
 __global__ void kv_append_kernel(const int8_t *__restrict__ src, int64_t lds, int k_col, int v_col,
                                  int8_t *__restrict__ kc, int8_t *__restrict__ vc, int B, int H, int T, int Tcap,
                                  int pos, const int32_t *pos_dev) {
+    pdl_wait();
+    pdl_launch();
     const int p0 = pos_dev ? *pos_dev : pos;
     const int64_t total = (int64_t)B * T * H * 16;  // int32 words per K (and per V)
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -634,8 +640,7 @@ cudaError_t kv_append(const int8_t *src, int64_t lds, int k_col, int v_col, int8
     if (total <= 0) return cudaSuccess;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 4096) blocks = 4096;
-    kv_append_kernel<<<(unsigned)blocks, 256, 0, st>>>(src, lds, k_col, v_col, kc, vc, B, H, T, Tcap, pos, pos_dev);
-    return cudaGetLastError();
+    return launch_pdl(kv_append_kernel, (unsigned)blocks, 256, 0, st, src, lds, k_col, v_col, kc, vc, B, H, T, Tcap, pos, pos_dev);
 }
 
 // ---------------------------------------------------------------------------
@@ -684,6 +689,8 @@ IW_DEV void block_best(int &q, int &i, int *qred, int *ired) {
 // smallest index, as torch.argmax). Every log-probability is then formed
 // with the same float operations as the per-token formula.
 __global__ void __launch_bounds__(kGreedyThreads) greedy_step_kernel(GreedyArgs g) {
+    pdl_wait();
+    pdl_launch();
     const int b = blockIdx.x;
     const int tid = threadIdx.x;
     __shared__ uint32_t hist[2][256];  // [0]: every allowed token, [1]: allowed timestamp tokens
@@ -778,15 +785,15 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_step_kernel(GreedyArgs 
 
 cudaError_t greedy_step(const GreedyArgs &g, int B, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
-    greedy_step_kernel<<<B, kGreedyThreads, 0, st>>>(g);
-    return cudaGetLastError();
+    return launch_pdl(greedy_step_kernel, B, kGreedyThreads, 0, st, g);
 }
 
-__global__ void add_i32_kernel(int32_t *p, int32_t v) { *p += v; }
+__global__ void add_i32_kernel(int32_t *p, int32_t v) {
+    pdl_wait();
+    pdl_launch(); *p += v; }
 
 cudaError_t add_i32(int32_t *p, int32_t v, cudaStream_t st) {
-    add_i32_kernel<<<1, 1, 0, st>>>(p, v);
-    return cudaGetLastError();
+    return launch_pdl(add_i32_kernel, 1, 1, 0, st, p, v);
 }
 
 // ---------------------------------------------------------------------------
