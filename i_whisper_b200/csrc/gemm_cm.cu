@@ -17,8 +17,8 @@
 //   warp 1      : TMEM allocation (2*BR columns) and the single-thread
 //                 tcgen05.mma 128xBRx32 issue loop, committing stages and
 //                 accumulator buffers.
-//   warps 2..9  : epilogue; warp w reads TMEM lane quadrant w%4 (32
-//                 channels) and every other 32-row chunk.
+//   warps 2..17 : epilogue; warp w reads TMEM lane quadrant w%4 (32
+//                 channels) and every fourth 16-row chunk.
 // Outputs: int8 row-major, int8 head-major (K/V caches), int8 transposed per
 // batch (V^T for the attention's P.V operand, or [B, N, T]), int16 after
 // Residual15, int16 after the positional add-requant; optional per-row sums
@@ -30,14 +30,14 @@
 
 namespace iw {
 
-template <int BR, bool GT>
+template <int BR, int GK>
 struct CmCfg {
     static constexpr int A_BYTES = 128 * kBlockK;  // W tile
     static constexpr int B_BYTES = BR * kBlockK;   // X tile
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int RS_BYTES = BR * 4;        // row sums of the tile's rows
     static constexpr int PART_BYTES = 4 * BR * 4;  // per-quadrant partial output row sums
-    static constexpr int GTAB_BYTES = GT ? 128 * 256 : 0;  // the tile's GeLU table, lane-interleaved
+    static constexpr int GTAB_BYTES = GK == 2 ? 128 * 256 : 0;  // the tile's GeLU table, lane-interleaved
     static constexpr int FIXED = 1024 + 256 + RS_BYTES + PART_BYTES + GTAB_BYTES;
     static constexpr int STAGES_FIT = (232448 - FIXED) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
@@ -45,6 +45,13 @@ struct CmCfg {
     static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
     static_assert(STAGES >= 3, "shared memory too small");
 };
+
+// Epilogue shape of this kernel: 16 warps (four per TMEM lane quadrant, so
+// four per SM sub-partition to hide latency) each taking 16-row chunks.
+constexpr int kCmEpiWarps = 16;
+constexpr int kCmCh = 16;
+constexpr int kCmThreads = 64 + 32 * kCmEpiWarps;
+IW_DEV void cm_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCmEpiWarps * 32) : "memory"); }
 
 // rounding_rshift(x, s) (fixedpoint.h:47-87) with the shift folded into
 // constants: s == 0 -> x, s >= 32 -> 0, otherwise
@@ -133,12 +140,15 @@ IW_DEV int32_t gelu_tab_k(int32_t x, const uint32_t *gw) {
     return (int32_t)(int8_t)(uint8_t)(w >> (b << 3));  // byte b, sign-extended
 }
 
-template <int BR, int MODE, bool GT>
-__global__ void __launch_bounds__(kThreads, 1)
+// GK: GeLU flavour of a Linear8 epilogue: 0 none, 1 from its parameters
+// (ALU), 2 from the per-channel lookup table.
+template <int BR, int MODE, int GK>
+__global__ void __launch_bounds__(kCmThreads, 1)
     gemm_cm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N,
                    int K, const EpiParams p) {
-    using Cfg = CmCfg<BR, GT>;
+    using Cfg = CmCfg<BR, GK>;
     constexpr int S = Cfg::STAGES;
+    constexpr bool GT = GK == 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
@@ -169,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kEpiWarps);
+            mbar_init(&tempty[b], kCmEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -248,10 +258,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int ew = warp - 2;
         const int quad = warp & 3;  // TMEM lane quadrant this warp may read
-        const int slice = ew >> 2;  // 0: even 32-row chunks, 1: odd ones
+        const int slice = ew >> 2;  // chunks slice, slice + 4, ...
         const int et = ew * 32 + lane;
         uint32_t lut[4] = {0, 0, 0, 0};
-        if (p.gelu) {
+        if (GK == 1) {
 #pragma unroll
             for (int w = 0; w < 4; ++w)
                 lut[w] = (uint32_t)p.lut[4 * w] | ((uint32_t)p.lut[4 * w + 1] << 8) |
@@ -265,14 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Barrier A: every epilogue warp is done with the previous tile's
             // shared row sums and partials. One thread samples the abort flag
             // so that all epilogue warps take the same decision.
-            epi_bar();
+            cm_bar();
             if (et == 0) *stop_s = *abort_flag;
-            for (int i = et; i < BR; i += kEpiWarps * 32)
+            for (int i = et; i < BR; i += kCmEpiWarps * 32)
                 rs_s[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
             if constexpr (GT) {
                 // 16 table bytes of one channel per thread; a warp covers 32
                 // consecutive channels, so the four word stores hit 32 banks
-                for (int i = et; i < 128 * 16; i += kEpiWarps * 32) {
+                for (int i = et; i < 128 * 16; i += kCmEpiWarps * 32) {
                     const int ch = i & 127, tq = i >> 7;
                     int4 t4 = make_int4(0, 0, 0, 0);
                     if (n0 + ch < N) t4 = __ldg(reinterpret_cast<const int4 *>(p.gelu_tab + (int64_t)(n0 + ch) * 256) + tq);
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     dst[96] = (uint32_t)t4.w;
                 }
             }
-            epi_bar();
+            cm_bar();
             if (*stop_s) break;
 
             const int n = n0 + quad * 32 + lane;
@@ -303,18 +313,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = slice; c < BR / 32; c += 2) {
-                    const int r0 = m0 + c * 32;
+                for (int c = slice; c < BR / kCmCh; c += kCmEpiWarps / 4) {
+                    const int r0 = m0 + c * kCmCh;
                     if (r0 >= M) break;  // warp-uniform
-                    uint32_t acc[32];
-                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BR + c * 32),
+                    uint32_t acc[kCmCh];
+                    tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BR + c * kCmCh),
                                        acc);
                     tmem_ld_wait();
-                    const int4 *rs4 = reinterpret_cast<const int4 *>(rs_s + c * 32);
-                    int32_t v[32];
+                    const int4 *rs4 = reinterpret_cast<const int4 *>(rs_s + c * kCmCh);
+                    int32_t v[kCmCh];
                     if (simple) {
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
+                        for (int q = 0; q < kCmCh / 4; ++q) {
                             const int4 r4 = rs4[q];
                             const int32_t rs[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
@@ -327,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     } else {
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
+                        for (int q = 0; q < kCmCh / 4; ++q) {
                             const int4 r4 = rs4[q];
                             const int32_t rs[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
@@ -351,12 +361,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // The residual is usually updated in place (res == out):
                             // load the chunk's 32 residuals before the first store so
                             // the loads overlap instead of waiting on each store.
-                            int32_t rv[32];
+                            int32_t rv[kCmCh];
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
+                            for (int j = 0; j < kCmCh; ++j)
                                 rv[j] = (r0 + j < M) ? (int32_t)p.res[(int64_t)(r0 + j) * p.ldr + n] : 0;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
+                            for (int j = 0; j < kCmCh; ++j) {
                                 const int64_t m = r0 + j;
                                 if (m < M) {
                                     int32_t t = u_mad(rv[j], rm, v[j]);
@@ -369,28 +379,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if constexpr (GT) {
                             const uint32_t *gw = gtab_s + quad * 2048 + 32 * 32 + lane;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = gelu_tab_k(v[j], gw);
-                        } else if (p.gelu) {
+                            for (int j = 0; j < kCmCh; ++j) v[j] = gelu_tab_k(v[j], gw);
+                        } else if constexpr (GK == 1) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = gelu_k(v[j], ck, lut);
+                            for (int j = 0; j < kCmCh; ++j) v[j] = gelu_k(v[j], ck, lut);
                         }
                         if (!cv) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = 0;
+                            for (int j = 0; j < kCmCh; ++j) v[j] = 0;
                         }
                         if (p.posadd) {
                             // add_requant15_scalar.cpp:29-80, int16 result
                             if (cv) {
                                 int16_t *out = reinterpret_cast<int16_t *>(p.out);
-                                int32_t pe[32];
+                                int32_t pe[kCmCh];
                                 int t = r0 % p.pe_T;
 #pragma unroll
-                                for (int j = 0; j < 32; ++j) {
+                                for (int j = 0; j < kCmCh; ++j) {
                                     pe[j] = (r0 + j < M) ? (int32_t)__ldg(p.pe + (int64_t)t * N + n) : 0;
                                     if (++t == p.pe_T) t = 0;
                                 }
 #pragma unroll
-                                for (int j = 0; j < 32; ++j) {
+                                for (int j = 0; j < kCmCh; ++j) {
                                     if (r0 + j < M) {
                                         const int32_t a = clampi(rrs_apply(wmul(v[j] + pe[j], ck.pm), ck.ps), -16383, 16383);
                                         out[(int64_t)(r0 + j) * p.ldo + n] = (int16_t)a;
@@ -404,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 const bool vec = (p.tr_T & 3) == 0 && (p.tr_ld & 3) == 0 &&
                                                  (reinterpret_cast<uintptr_t>(p.tr_out) & 3) == 0;
 #pragma unroll
-                                for (int j = 0; j < 32; j += 4) {
+                                for (int j = 0; j < kCmCh; j += 4) {
                                     const int m = r0 + j;
                                     if (vec && m + 3 < M) {
                                         int8_t *dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
@@ -430,20 +440,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 int8_t *base = reinterpret_cast<int8_t *>(p.out) + (int64_t)(n >> 6) * p.hm_B * p.hm_T * 64 +
                                                (n & 63);
 #pragma unroll
-                                for (int j = 0; j < 32; ++j)
+                                for (int j = 0; j < kCmCh; ++j)
                                     if (r0 + j < M) base[(int64_t)(r0 + j) * 64] = (int8_t)v[j];
                             }
                         } else if (cv) {
                             int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
                             if (r0 + 32 <= M) {
 #pragma unroll
-                                for (int j = 0; j < 32; ++j) {
+                                for (int j = 0; j < kCmCh; ++j) {
                                     *out = (int8_t)v[j];
                                     out += p.ldo;
                                 }
                             } else {
 #pragma unroll
-                                for (int j = 0; j < 32; ++j) {
+                                for (int j = 0; j < kCmCh; ++j) {
                                     if (r0 + j < M) *out = (int8_t)v[j];
                                     out += p.ldo;
                                 }
@@ -451,13 +461,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         if (p.rowsum_out) {
                             // per row, the sum over this warp's 32 channels
-                            int32_t rsum[32];
+                            int32_t rsum[kCmCh];
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) rsum[j] = __reduce_add_sync(0xffffffffu, v[j]);
+                            for (int j = 0; j < kCmCh; ++j) rsum[j] = __reduce_add_sync(0xffffffffu, v[j]);
                             if (lane == 0) {
-                                int4 *dst = reinterpret_cast<int4 *>(part + quad * BR + c * 32);
+                                int4 *dst = reinterpret_cast<int4 *>(part + quad * BR + c * kCmCh);
 #pragma unroll
-                                for (int q4 = 0; q4 < 8; ++q4)
+                                for (int q4 = 0; q4 < kCmCh / 4; ++q4)
                                     dst[q4] = make_int4(rsum[4 * q4], rsum[4 * q4 + 1], rsum[4 * q4 + 2], rsum[4 * q4 + 3]);
                             }
                         }
@@ -471,8 +481,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (buf == 0) bphase ^= 1;
             if (MODE == EPI_L8 && p.rowsum_out) {
                 // Barrier C: all four quadrants' partial sums of each row are in.
-                epi_bar();
-                for (int i = et; i < BR; i += kEpiWarps * 32)
+                cm_bar();
+                for (int i = et; i < BR; i += kCmEpiWarps * 32)
                     if (m0 + i < M)
                         atomicAdd(p.rowsum_out + m0 + i, part[i] + part[BR + i] + part[2 * BR + i] + part[3 * BR + i]);
             }
@@ -487,9 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BR, int MODE, bool GT>
+template <int BR, int MODE, int GK>
 static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStream_t stream) {
-    using Cfg = CmCfg<BR, GT>;
+    using Cfg = CmCfg<BR, GK>;
     CUtensorMap tw, tx;
     cudaError_t e = make_tmap_2d_u8(&tw, g.w, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.ldw, kBlockK, 128);
     if (e != cudaSuccess) return e;
@@ -497,20 +507,20 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
     if (e != cudaSuccess) return e;
     static bool attr_set = false;
     if (!attr_set) {
-        e = cudaFuncSetAttribute(gemm_cm_kernel<BR, MODE, GT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        e = cudaFuncSetAttribute(gemm_cm_kernel<BR, MODE, GK>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const long tiles = (long)((g.N + 127) / 128) * ((g.M + BR - 1) / BR);
     const int grid = tiles < num_sms() ? (int)tiles : num_sms();
-    return launch_pdl(gemm_cm_kernel<BR, MODE, GT>, grid, kThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K, p);
+    return launch_pdl(gemm_cm_kernel<BR, MODE, GK>, grid, kCmThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K, p);
 }
 
-template <int MODE, bool GT>
+template <int MODE, int GK>
 static cudaError_t launch_cm_mode(const GemmShape &g, const EpiParams &p, cudaStream_t stream, int br) {
-    if (br == 64) return launch_cm_t<64, MODE, GT>(g, p, stream);
-    if (br == 128) return launch_cm_t<128, MODE, GT>(g, p, stream);
-    return launch_cm_t<256, MODE, GT>(g, p, stream);
+    if (br == 64) return launch_cm_t<64, MODE, GK>(g, p, stream);
+    if (br == 128) return launch_cm_t<128, MODE, GK>(g, p, stream);
+    return launch_cm_t<256, MODE, GK>(g, p, stream);
 }
 
 // The channel-major path covers Linear8 (per-channel or scalar requant,
@@ -540,10 +550,11 @@ cudaError_t gemm_cm_launch(const GemmShape &g, EpiMode mode, const EpiParams &p,
         if (ch_tiles * ((g.M + 127) / 128) < num_sms() / 2) br = 64;
     }
     if (mode == EPI_L8) {
-        if (p.gelu_tab) return launch_cm_mode<EPI_L8, true>(g, p, stream, br);
-        return launch_cm_mode<EPI_L8, false>(g, p, stream, br);
+        if (p.gelu_tab) return launch_cm_mode<EPI_L8, 2>(g, p, stream, br);
+        if (p.gelu) return launch_cm_mode<EPI_L8, 1>(g, p, stream, br);
+        return launch_cm_mode<EPI_L8, 0>(g, p, stream, br);
     }
-    return launch_cm_mode<EPI_L32_RES, false>(g, p, stream, br);
+    return launch_cm_mode<EPI_L32_RES, 0>(g, p, stream, br);
 }
 
 }  // namespace iw
