@@ -53,22 +53,6 @@ constexpr int kCmCh = 16;
 constexpr int kCmThreads = 64 + 32 * kCmEpiWarps;
 IW_DEV void cm_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCmEpiWarps * 32) : "memory"); }
 
-// rounding_rshift(x, s) (fixedpoint.h:47-87) with the shift folded into
-// constants: s == 0 -> x, s >= 32 -> 0, otherwise
-// (int32)((u32)x + 2^(s-1) - (x < 0)) >> s.
-struct RrsK {
-    int32_t rnd, sgn, sh, z;
-};
-IW_DEV RrsK rrs_k(uint32_t s) {
-    if (s == 0) return {0, 0, 0, -1};
-    if (s < 32) return {(int32_t)(1u << (s - 1)), -1, (int32_t)s, -1};
-    return {0, 0, 0, 0};
-}
-IW_DEV int32_t rrs_apply(int32_t x, const RrsK &k) {
-    const int32_t t = u_add(u_add(x, k.rnd), (x >> 31) & k.sgn);
-    return (t >> k.sh) & k.z;
-}
-
 // Everything the epilogue needs about its channel, loaded once per tile.
 struct ChanK {
     int32_t bias, nwz, mul, hmask;  // acc + bias - wz*rowsum; mulh by u32 multiplier

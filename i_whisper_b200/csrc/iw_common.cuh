@@ -99,6 +99,22 @@ IW_DEV int32_t gelu_one(int32_t x, const uint8_t *lut, uint32_t mi, uint32_t si,
     return clampi(v, -127, 127);
 }
 
+// rounding_rshift(x, s) (fixedpoint.h:47-87) with the shift folded into
+// constants: s == 0 -> x, s >= 32 -> 0, otherwise
+// (int32)((u32)x + 2^(s-1) - (x < 0)) >> s.
+struct RrsK {
+    int32_t rnd, sgn, sh, z;
+};
+IW_DEV RrsK rrs_k(uint32_t s) {
+    if (s == 0) return {0, 0, 0, -1};
+    if (s < 32) return {(int32_t)(1u << (s - 1)), -1, (int32_t)s, -1};
+    return {0, 0, 0, 0};
+}
+IW_DEV int32_t rrs_apply(int32_t x, const RrsK &k) {
+    const int32_t t = wadd(wadd(x, k.rnd), (x >> 31) & k.sgn);
+    return (t >> k.sh) & k.z;
+}
+
 // attention_scalar.cpp:388-560 -- shift-based exp2 of (x - rowmax1) in
 // int16 wrapping arithmetic. The caller handles masked lanes.
 IW_DEV int32_t shift_exp_one(int32_t x, int32_t xm, int32_t fb) {
