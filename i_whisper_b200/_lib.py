@@ -90,7 +90,7 @@ class AttnDesc(C.Structure):
         ("Tk_dev", _P), ("Tk_cap", _I64), ("mask_mode", C.c_int), ("mask", _P),
         ("qk_multiplier", _U8), ("qk_shift", _I8), ("frac_bits", _I32),
         ("av_multiplier", _U8), ("av_shift", _I8), ("rsqrt_offset", _I32),
-        ("exp_table", _P), ("vt", _P), ("vt_ld", _I64), ("vt_ready", C.c_int),
+        ("exp_table", _P), ("vt", _P), ("vt_ld", _I64), ("vt_ready", C.c_int), ("row_sum_out", _P),
     ]
 
 

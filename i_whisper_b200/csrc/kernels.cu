@@ -602,17 +602,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     }
     __syncthreads();
     const uint32_t avs = (uint32_t)clampi(a.av_shift, 0, 32);
-    for (int idx = tid; idx < QB * 64; idx += kAttnThreads) {
-        const int r = idx / 64, d = idx % 64;
-        if (r >= nq) continue;
-        uint32_t sum = 0;
+    static_assert(QB * 64 <= kAttnThreads, "one output value per thread");
+    if (tid < QB * 64) {
+        const int r = tid / 64, d = tid % 64;  // r is uniform within a warp
+        int32_t o = 0;
+        if (r < nq) {
+            uint32_t sum = 0;
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) sum += (uint32_t)pv_part[w][r][d];
-        const int32_t inv = fisr(rowv[r][1], a.rsqrt_offset);
-        int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
-        v = rrs(wmul(v, inv), a.rsqrt_offset);
-        v = rrs(wmul(v, (int32_t)a.av_mult), avs);
-        a.out[(int64_t)b * a.o_bs + (int64_t)(q0 + r) * a.ldo + (int64_t)h * a.o_hs + d] = (int8_t)clampi(v, -127, 127);
+            for (int w = 0; w < kAttnWarps; ++w) sum += (uint32_t)pv_part[w][r][d];
+            const int32_t inv = fisr(rowv[r][1], a.rsqrt_offset);
+            int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
+            v = rrs(wmul(v, inv), a.rsqrt_offset);
+            v = rrs(wmul(v, (int32_t)a.av_mult), avs);
+            o = clampi(v, -127, 127);
+            a.out[(int64_t)b * a.o_bs + (int64_t)(q0 + r) * a.ldo + (int64_t)h * a.o_hs + d] = (int8_t)o;
+        }
+        if (a.rowsum_out) {
+            // this head's share of the output row's sum (the next GEMM's
+            // zero-point term), added to rowsum_out[b*Tq + q]
+            const int32_t s = warp_sum(o);
+            if (lane == 0 && r < nq) atomicAdd(a.rowsum_out + (int64_t)b * Tq + q0 + r, s);
+        }
     }
 }
 

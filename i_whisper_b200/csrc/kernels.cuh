@@ -46,6 +46,7 @@ struct AttnArgs {
     uint32_t av_mult;
     int32_t av_shift;
     uint32_t rsqrt_offset;
+    int32_t *rowsum_out = nullptr;  // optional: += sum of each output row, index b*Tq + q
 };
 
 cudaError_t rowsum_i8(const int8_t *x, int64_t ldx, int M, int K, int32_t *out, cudaStream_t st);
