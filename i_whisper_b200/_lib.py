@@ -76,6 +76,8 @@ class GemmDesc(C.Structure):
         ("transpose_T", _I64), ("headmajor_T", _I64), ("headmajor_B", _I64),
         ("out_rowsum", _P), ("tile_n", C.c_int), ("gelu_table", _P),
         ("vt_out", _P), ("vt_ld", _I64), ("vt_col0", _I64), ("vt_T", _I64),
+        ("kv_cache_k", _P), ("kv_cache_v", _P), ("kv_col0", _I64), ("kv_heads", _I64), ("kv_T", _I64),
+        ("kv_Tcap", _I64), ("kv_pos", _I64), ("kv_pos_dev", _P),
     ]
 
 

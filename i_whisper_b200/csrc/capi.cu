@@ -421,6 +421,32 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     p.hm_B = (int)d->headmajor_B;
     p.rowsum_out = d->out_rowsum;
     p.gelu_tab = d->gelu_table;
+    if (d->kv_cache_k) {
+        if (!d->kv_cache_v || d->mode != IW_GEMM_INT8 || d->vt_out || d->headmajor_T || d->transpose_T || d->pos ||
+            d->kv_heads <= 0 || d->kv_T <= 0 || d->M % d->kv_T || d->kv_col0 < 0 || d->kv_col0 % 64 ||
+            d->kv_col0 + 2 * d->kv_heads * 64 != d->N || d->kv_Tcap < d->kv_T ||
+            (!d->kv_pos_dev && (d->kv_pos < 0 || d->kv_pos + d->kv_T > d->kv_Tcap)))
+            return fail(IW_EINVAL, "iw_gemm_i8: invalid KV-cache output");
+        if (!iw::cm_enabled()) {
+            // row-major kernel: all channels row-major, then the cache append
+            iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
+            if (int r = cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8"))
+                return r;
+            const int64_t kc = d->kv_col0, vc = d->kv_col0 + d->kv_heads * 64;
+            return cuda_check(iw::kv_append(reinterpret_cast<const int8_t *>(d->out), d->ldo, (int)kc, (int)vc,
+                                            d->kv_cache_k, d->kv_cache_v, (int)(d->M / d->kv_T), (int)d->kv_heads,
+                                            (int)d->kv_T, (int)d->kv_Tcap, (int)d->kv_pos, d->kv_pos_dev, S(stream)),
+                              "iw_gemm_i8");
+        }
+        p.kv_k = d->kv_cache_k;
+        p.kv_v = d->kv_cache_v;
+        p.kv_c0 = (int)d->kv_col0;
+        p.kv_H = (int)d->kv_heads;
+        p.kv_T = (int)d->kv_T;
+        p.kv_Tcap = (int)d->kv_Tcap;
+        p.kv_pos = (int)d->kv_pos;
+        p.kv_pos_dev = d->kv_pos_dev;
+    }
     if (d->vt_out && !iw::cm_enabled()) {
         // row-major kernel: all channels row-major, then V^T by a transpose
         iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};

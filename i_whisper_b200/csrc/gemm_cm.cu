@@ -284,6 +284,13 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             const bool cv = n < N;
             const ChanK ck = load_chan(p, n, cv, MODE);
             const bool to_tr = p.tr_out && n >= p.tr_c0;
+            const bool to_kv = p.kv_k && n >= p.kv_c0;
+            int8_t *kv_base = nullptr;
+            if (to_kv) {
+                const int c = n - p.kv_c0, hd = p.kv_H * 64;
+                const int pos = p.kv_pos_dev ? *p.kv_pos_dev : p.kv_pos;
+                kv_base = (c < hd ? p.kv_k : p.kv_v) + ((int64_t)((c % hd) >> 6) * p.kv_Tcap + pos) * 64 + (c & 63);
+            }
             // Checkpoints made by the quantiser's frexp rule have multipliers
             // below 2^31 and shifts in [1, 31]; for such a warp the MULH needs
             // no correction and the rounding shift is three instructions.
@@ -418,6 +425,17 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                     }
                                 }
                             }
+                        } else if (to_kv) {
+                            // self-attention K/V cache rows at the current position
+                            if (cv) {
+                                int b = r0 / p.kv_T, t = r0 - (r0 / p.kv_T) * p.kv_T;
+#pragma unroll
+                                for (int j = 0; j < kCmCh; ++j) {
+                                    if (r0 + j < M)
+                                        kv_base[((int64_t)b * p.kv_H * p.kv_Tcap + t) * 64] = (int8_t)v[j];
+                                    if (++t == p.kv_T) { t = 0; ++b; }
+                                }
+                            }
                         } else if (p.hm_T) {
                             // head-major K/V cache rows
                             if (cv) {
@@ -429,7 +447,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             }
                         } else if (cv) {
                             int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
-                            if (r0 + 32 <= M) {
+                            if (r0 + kCmCh <= M) {
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
                                     *out = (int8_t)v[j];
@@ -522,6 +540,7 @@ bool cm_eligible(const GemmShape &g, EpiMode mode, const EpiParams &p) {
         return false;
     if (mode == EPI_L32_RES && (reinterpret_cast<uintptr_t>(p.out) & 1)) return false;
     if (p.posadd && (p.hm_T || p.tr_out || p.rowsum_out)) return false;
+    if (p.kv_k && (p.posadd || p.hm_T || p.tr_out || p.kv_T <= 0)) return false;
     if (p.tr_out && (p.tr_T <= 0 || p.tr_N <= 0)) return false;
     return true;
 }

@@ -71,6 +71,13 @@ struct EpiParams {
     int8_t *tr_out = nullptr;
     int tr_c0 = 0, tr_N = 0, tr_T = 0;
     int64_t tr_ld = 0;
+    // optional (channel-major path): channels n >= kv_c0 hold the keys then
+    // the values of self-attention (2 * kv_H * 64 channels), written into the
+    // head-major caches [B, kv_H, kv_Tcap, 64] at position (*kv_pos_dev, or
+    // kv_pos) + t for row m = b * kv_T + t, instead of row-major
+    int8_t *kv_k = nullptr, *kv_v = nullptr;
+    int kv_c0 = 0, kv_H = 0, kv_T = 0, kv_Tcap = 0, kv_pos = 0;
+    const int32_t *kv_pos_dev = nullptr;
 };
 
 // Builds tab[n][x+128] = GeLU_n(x) for x in [-128, 127] (gelu_scalar.cpp).

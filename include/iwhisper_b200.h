@@ -230,6 +230,17 @@ typedef struct iw_gemm_desc {
     int64_t vt_ld;
     int64_t vt_col0;
     int64_t vt_T;
+    /* optional self-attention KV-cache output (replaces iw_kv_append after
+     * the fused QKV projection): int8 results of channels kv_col0 ..
+     * kv_col0 + 2*kv_heads*64 - 1 (keys, then values) go to the head-major
+     * caches [B, kv_heads, kv_Tcap, 64] at position p + t for row
+     * m = b*kv_T + t, with p = *kv_pos_dev when kv_pos_dev != NULL, else
+     * kv_pos; the caller keeps p + kv_T <= kv_Tcap. Those channels are not
+     * written to out. kv_col0 + 2*kv_heads*64 == N, kv_col0 % 64 == 0. */
+    int8_t *kv_cache_k;
+    int8_t *kv_cache_v;
+    int64_t kv_col0, kv_heads, kv_T, kv_Tcap, kv_pos;
+    const int32_t *kv_pos_dev;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */

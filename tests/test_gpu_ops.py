@@ -511,3 +511,44 @@ def test_greedy_step(n_hist):
     st = host(d_state)
     assert np.array_equal(st[:, 0], np.full(B, n_hist + 1))
     assert np.array_equal(st[:, 1], want.numpy())
+
+
+@pytest.mark.parametrize("B,T,H,pos,dev_pos", [(3, 1, 6, 5, False), (2, 3, 16, 0, False), (4, 1, 8, 447, True),
+                                               (256, 1, 16, 100, True)])
+def test_linear8_kv_cache_out(ops, L, B, T, H, pos, dev_pos):
+    """Decoder QKV form: Q row-major, K and V written by the GEMM into the
+    head-major self-attention caches at the current position (what
+    iw_kv_append does after a plain projection)."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(B * 31 + T + H + pos)
+    d_, Tcap = H * 64, 448
+    K, N, M = d_, 3 * d_, B * T
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N)
+    ref = L.linear8(x, w, b, wz, m, s)
+    X, W = dev(x), dev(w)
+    rs = torch.from_numpy(x.astype(np.int32).sum(1).astype(np.int32)).cuda()
+    out = torch.zeros(M, N, dtype=torch.int8, device="cuda")
+    kc0 = rng.integers(-127, 128, (B, H, Tcap, 64), dtype=np.int8)
+    vc0 = rng.integers(-127, 128, (B, H, Tcap, 64), dtype=np.int8)
+    kc, vc = dev(kc0), dev(vc0)
+    pos_t = dev(np.array([pos], np.int32))
+    B_, Z, Mu, S_ = dev(b), dev(wz), dev(m), dev(s)
+    g = _lib.GemmDesc()
+    g.x, g.ldx, g.w, g.ldw, g.M, g.N, g.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    g.mode, g.out, g.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
+    g.bias, g.weight_zero, g.x_rowsum, g.multiplier, g.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    g.kv_cache_k, g.kv_cache_v, g.kv_col0, g.kv_heads, g.kv_T, g.kv_Tcap = kc.data_ptr(), vc.data_ptr(), d_, H, T, Tcap
+    if dev_pos:
+        g.kv_pos, g.kv_pos_dev = -1, pos_t.data_ptr()
+    else:
+        g.kv_pos = pos
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(g), torch.cuda.current_stream().cuda_stream))
+    assert np.array_equal(host(out)[:, :d_], ref[:, :d_])
+    want_k, want_v = kc0.copy(), vc0.copy()
+    kk = ref[:, d_:2 * d_].reshape(B, T, H, 64).transpose(0, 2, 1, 3)
+    vv = ref[:, 2 * d_:].reshape(B, T, H, 64).transpose(0, 2, 1, 3)
+    want_k[:, :, pos:pos + T] = kk
+    want_v[:, :, pos:pos + T] = vv
+    assert np.array_equal(host(kc), want_k)
+    assert np.array_equal(host(vc), want_v)
