@@ -75,3 +75,21 @@ def test_model_matches_oracle(dims, seed, mel_seeds, steps):
 def test_device_status_clean_after_model():
     from i_whisper_b200 import _lib
     assert _lib.device_status(clear=True) == 0
+
+
+def test_encode_batches_pipelined():
+    """The host-buffer streaming API (uploads and downloads overlapping the
+    neighbouring batches' compute) returns, batch for batch, what the
+    device-resident encoder returns."""
+    from i_whisper_b200.model import WhisperIntB200
+    dims = ModelDims(80, 1500, 384, 6, 1, 51865, 448, 384, 6, 1)
+    sd = synthetic_state_dict(dims, 3)
+    alpha = float(sd["encoder.input_alpha"][0])
+    model = WhisperIntB200(dims, sd)
+    mels = [torch.from_numpy(synthetic_mel_batch(dims.n_mels, [s, s + 1], alpha)).pin_memory() for s in (0, 2, 4, 6, 8)]
+    outs = [torch.empty(2, dims.n_audio_ctx, dims.n_audio_state, dtype=torch.int8).pin_memory() for _ in mels]
+    model.encode_batches(mels, outs)
+    torch.cuda.synchronize()
+    for m, o in zip(mels, outs):
+        want = model.encoder(m.cuda()).cpu()
+        assert torch.equal(o, want)
