@@ -17,6 +17,7 @@ IW_EINVAL = -1
 IW_EVALUE = -2
 IW_ECUDA = -3
 IW_EDEVICE = -4
+IW_EOVERFLOW = -5
 
 _P = C.c_void_p
 _I64 = C.c_int64
@@ -31,6 +32,9 @@ SIGNATURES = {
     "iw_residual15": [_P, _P, _U16, _P, _I64, _P],
     "iw_layernorm32": [_P, _P, _P, _U8, _I8, _U32, _I8, _P, _I64, _I64, _P],
     "iw_layernorm32_stats": [_P, _P, _P, _P, _I64, _I64, _P],
+    "iw_layernorm64": [_P, _P, _P, _U8, _I8, _U32, _I8, _P, _I64, _I64, _P],
+    "iw_layernorm64_stats": [_P, _P, _P, _I64, _I64, _P],
+    "iw_layernorm64_ex": [_P, _I64, _P, _P, _U8, _I8, _U32, _I8, _P, _I64, _I64, _I64, _P, _P, _P],
     "iw_layernorm32_rsqrt": [_P, _P, _I64, _P],
     "iw_gelu": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P],
     "iw_qk_requant_rowmax": [_P, _P, _P, _U8, _I8, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
@@ -137,6 +141,8 @@ def check(rc: int):
     msg = last_error()
     if rc == IW_EVALUE:
         raise ValueError(msg)
+    if rc == IW_EOVERFLOW:
+        raise OverflowError(msg)
     raise IWhisperError(msg)
 
 

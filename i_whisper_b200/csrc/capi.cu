@@ -539,6 +539,52 @@ int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const
         "iw_layernorm32_ex");
 }
 
+// layernorm_torch.cpp:446-460: LayerNorm64 runs FISR with offset 15 and
+// adds 2 to the normalise shift
+static iw::LnParams ln64_params(uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift) {
+    iw::LnParams p{(int32_t)ln_multiplier, (int32_t)ln_shift, out_multiplier, (uint32_t)(int32_t)out_shift, 15u};
+    p.additional_offset = 2;
+    return p;
+}
+
+int iw_layernorm64(const int16_t *x, const int8_t *weight, const int32_t *bias, uint8_t ln_multiplier,
+                   int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y, int64_t rows, int64_t d,
+                   void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    if (rows < 0 || rows > INT32_MAX) return fail(IW_EINVAL, "iw_layernorm64: invalid row count");
+    if (rows == 0) return IW_OK;
+    cudaStream_t st = S(stream);
+    Scratch f(st);
+    if (int r = cuda_check(f.alloc(sizeof(int)), "iw_layernorm64")) return r;
+    if (int r = cuda_check(cudaMemsetAsync(f.p, 0, sizeof(int), st), "iw_layernorm64")) return r;
+    iw::LnParams p = ln64_params(ln_multiplier, ln_shift, out_multiplier, out_shift);
+    p.overflow = (int *)f.p;
+    if (int r = cuda_check(iw::layernorm32(x, d, weight, bias, p, y, d, (int)rows, (int)d, nullptr, nullptr, st, true),
+                           "iw_layernorm64"))
+        return r;
+    int h = 0;
+    if (int r = cuda_check(cudaMemcpyAsync(&h, f.p, sizeof(int), cudaMemcpyDeviceToHost, st), "iw_layernorm64")) return r;
+    if (int r = cuda_check(cudaStreamSynchronize(st), "iw_layernorm64")) return r;
+    if (h) return fail(IW_EOVERFLOW, "LayerNorm64 variance does not fit INT32");
+    return IW_OK;
+}
+
+int iw_layernorm64_stats(const int16_t *x, int32_t *mean, int64_t *variance, int64_t rows, int64_t d, void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    if (rows < 0 || rows > INT32_MAX) return fail(IW_EINVAL, "iw_layernorm64_stats: invalid row count");
+    return cuda_check(iw::layernorm64_stats(x, (int)rows, (int)d, mean, variance, S(stream)), "iw_layernorm64_stats");
+}
+
+int iw_layernorm64_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
+                      uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
+                      int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream) {
+    if (!ln_width_ok(d)) return fail(IW_EINVAL, "unsupported LayerNorm hidden size: %lld", (long long)d);
+    const iw::LnParams p = ln64_params(ln_multiplier, ln_shift, out_multiplier, out_shift);
+    return cuda_check(
+        iw::layernorm32(x, ldx, weight, bias, p, y, ldy, (int)rows, (int)d, rowsum_out, rowsum_zero, S(stream), true),
+        "iw_layernorm64_ex");
+}
+
 int iw_im2col(const int8_t *x, int8_t *out, int64_t B, int64_t Cin, int64_t Tin, int64_t K, int64_t stride,
               int64_t pad, int64_t Tout, int64_t ldo, int channels_last, void *stream) {
     if (ldo < Cin * K) return fail(IW_EINVAL, "iw_im2col: ldo < Cin*K");

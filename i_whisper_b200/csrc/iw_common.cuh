@@ -153,6 +153,7 @@ IW_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: 
 enum : uint32_t {
     IW_DEVERR_NONE = 0,
     IW_DEVERR_WAIT_TIMEOUT = 1u << 0,
+    IW_DEVERR_LN64_OVERFLOW = 1u << 1,  // a LayerNorm64 variance did not fit INT32
 };
 
 // The library is built as one translation unit (iw_lib.cu), so this single

@@ -54,6 +54,16 @@ IW_DEV int32_t norm_reduce(int32_t x) {
     else return (x + (x >> 1)) >> 11;  // 1280
 }
 
+template <int D>
+IW_DEV int64_t norm_reduce64(int64_t x) {
+    // layernorm_scalar.cpp:58-90 (LayerNorm64)
+    if constexpr (D == 384) return (x + (x >> 2) + (x >> 3)) >> 9;
+    else if constexpr (D == 512) return x >> 9;
+    else if constexpr (D == 768) return (x + (x >> 2) + (x >> 3)) >> 10;
+    else if constexpr (D == 1024) return x >> 10;
+    else return (x + (x >> 1)) >> 11;  // 1280
+}
+
 IW_DEV int32_t warp_sum(int32_t v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -65,8 +75,11 @@ IW_DEV int32_t warp_max(int32_t v) {
     return v;
 }
 
-template <int D>
-__global__ void __launch_bounds__(256) layernorm32_kernel(const int16_t *__restrict__ x, int64_t ldx,
+// L64: the LayerNorm64 research variant (layernorm_scalar.cpp:626-825):
+// int64 sum of the unshifted centred squares, FISR of that variance, and the
+// normalise shift ln_shift + additional_offset; the element chain is shared.
+template <int D, bool L64>
+__global__ void __launch_bounds__(256) layernorm_kernel(const int16_t *__restrict__ x, int64_t ldx,
                                                            const int8_t *__restrict__ gamma,
                                                            const int32_t *__restrict__ beta, LnParams p,
                                                            int8_t *__restrict__ y, int64_t ldy, int rows,
@@ -93,29 +106,59 @@ __global__ void __launch_bounds__(256) layernorm32_kernel(const int16_t *__restr
     for (int i = 0; i < G * 4; ++i) s += v[i];
     s = warp_sum(s);
     const int32_t mean = norm_reduce<D>(s);
-    // |x - mean| < 2^15 for INT15 inputs, so the squares are exact and
-    // non-negative: rounding_rshift by the even renorm shift rs needs no sign
-    // term, and rs <= 16.
-    int32_t mx = 0;
-    int32_t sq[G * 4];
+    int32_t inv;
+    uint32_t nshift;
+    if constexpr (!L64) {
+        // The reference squares in int32 (centered_square, wrapping for
+        // |x - mean| > 46340). For INT15 rows every square is exact and
+        // non-negative and the rounding shift by the even renorm shift rs
+        // (<= 16) needs no sign term; a row with a wrapped (negative) square
+        // takes the signed form.
+        int32_t mx = 0, mn = 0;
+        int32_t sq[G * 4];
 #pragma unroll
-    for (int i = 0; i < G * 4; ++i) {
-        v[i] -= mean;
-        sq[i] = v[i] * v[i];
-        mx = max(mx, sq[i]);
+        for (int i = 0; i < G * 4; ++i) {
+            v[i] -= mean;
+            sq[i] = wmul(v[i], v[i]);
+            mx = max(mx, sq[i]);
+            mn = min(mn, sq[i]);
+        }
+        mx = warp_max(mx);
+        const bool wrapped = __any_sync(0xffffffffu, mn < 0);
+        int32_t rs = bit_length_nonneg(mx) - 16;
+        rs = rs < 0 ? 0 : rs;
+        rs = (rs + 1) & ~1;
+        const int32_t rs_rnd = rs ? (1 << (rs - 1)) : 0;
+        int32_t vs = 0;
+        if (!wrapped) {
+#pragma unroll
+            for (int i = 0; i < G * 4; ++i) vs = wadd(vs, (sq[i] + rs_rnd) >> rs);
+        } else {
+#pragma unroll
+            for (int i = 0; i < G * 4; ++i) vs = wadd(vs, rrs(sq[i], (uint32_t)rs));
+        }
+        vs = warp_sum(vs);
+        const int32_t var = norm_reduce<D>(vs);
+        inv = fisr(var, p.rsqrt_offset);
+        nshift = (uint32_t)(p.ln_shift + (rs >> 1));
+    } else {
+        // |x - mean| <= 65535, so each square fits uint32 exactly
+        uint64_t vs = 0;
+#pragma unroll
+        for (int i = 0; i < G * 4; ++i) {
+            v[i] -= mean;
+            vs += (uint64_t)((uint32_t)v[i] * (uint32_t)v[i]);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+        const int64_t var64 = norm_reduce64<D>((int64_t)vs);
+        if (var64 > (int64_t)INT32_MAX && lane == 0) {
+            if (p.overflow) atomicExch(p.overflow, 1);
+            else atomicOr(&g_device_status, IW_DEVERR_LN64_OVERFLOW);
+        }
+        inv = fisr((int32_t)var64, p.rsqrt_offset);
+        nshift = (uint32_t)(p.ln_shift + p.additional_offset);
     }
-    mx = warp_max(mx);
-    int32_t rs = bit_length_nonneg(mx) - 16;
-    rs = rs < 0 ? 0 : rs;
-    rs = (rs + 1) & ~1;
-    const int32_t rs_rnd = rs ? (1 << (rs - 1)) : 0;
-    int32_t vs = 0;
-#pragma unroll
-    for (int i = 0; i < G * 4; ++i) vs = wadd(vs, (sq[i] + rs_rnd) >> rs);
-    vs = warp_sum(vs);
-    const int32_t var = norm_reduce<D>(vs);
-    const int32_t inv = fisr(var, p.rsqrt_offset);
-    const uint32_t nshift = (uint32_t)(p.ln_shift + (rs >> 1));
     // (v * inv) * ln_mult wraps mod 2^32 like v * (inv * ln_mult)
     const int32_t kmul = wmul(inv, p.ln_mult);
     const RrsK kn = rrs_k(nshift);
@@ -172,7 +215,7 @@ __global__ void __launch_bounds__(256) layernorm32_kernel(const int16_t *__restr
 
 cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, const int32_t *beta, const LnParams &p,
                         int8_t *y, int64_t ldy, int rows, int d, int32_t *rowsum_out, int32_t *rowsum_zero,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool l64) {
     if (rows <= 0) return cudaSuccess;
     if ((reinterpret_cast<uintptr_t>(x) & 7) || (ldx & 3) || (reinterpret_cast<uintptr_t>(y) & 3) || (ldy & 3) ||
         (reinterpret_cast<uintptr_t>(gamma) & 3) || (beta && (reinterpret_cast<uintptr_t>(beta) & 15)))
@@ -181,10 +224,13 @@ cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, cons
     // spread over more SMs with one warp per sub-partition
     const int threads = rows < 8192 ? 128 : 256;
     const int blocks = (rows * 32 + threads - 1) / threads;
-#define IW_LN_CASE(DD)                                                                                      \
-    case DD:                                                                                                \
-        return launch_pdl(layernorm32_kernel<DD>, blocks, threads, 0, st, x, ldx, gamma, beta, p, y, ldy, rows, \
-                          rowsum_out, rowsum_zero);
+#define IW_LN_CASE(DD)                                                                                        \
+    case DD:                                                                                                  \
+        if (l64)                                                                                              \
+            return launch_pdl(layernorm_kernel<DD, true>, blocks, threads, 0, st, x, ldx, gamma, beta, p, y, ldy, \
+                              rows, rowsum_out, rowsum_zero);                                                 \
+        return launch_pdl(layernorm_kernel<DD, false>, blocks, threads, 0, st, x, ldx, gamma, beta, p, y, ldy,    \
+                          rows, rowsum_out, rowsum_zero);
     switch (d) {
         IW_LN_CASE(384)
         IW_LN_CASE(512)
@@ -249,6 +295,51 @@ cudaError_t layernorm32_stats(const int16_t *x, int rows, int d, int32_t *mean, 
                               cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     ln_stats_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, rows, d, mean, var, rs);
+    return cudaGetLastError();
+}
+
+// LayerNorm64 statistics (layernorm_scalar.cpp:230-297): the LayerNorm32
+// mean and the width-divided int64 sum of unshifted centred squares.
+__global__ void ln64_stats_kernel(const int16_t *__restrict__ x, int rows, int d, int32_t *mean_o, int64_t *var_o) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int16_t *xr = x + (int64_t)row * d;
+    int32_t s = 0;
+    for (int c = lane; c < d; c += 32) s += xr[c];
+    s = warp_sum(s);
+    int32_t mean;
+    switch (d) {
+    case 384: mean = norm_reduce<384>(s); break;
+    case 512: mean = norm_reduce<512>(s); break;
+    case 768: mean = norm_reduce<768>(s); break;
+    case 1024: mean = norm_reduce<1024>(s); break;
+    default: mean = norm_reduce<1280>(s); break;
+    }
+    uint64_t vs = 0;
+    for (int c = lane; c < d; c += 32) {
+        const int32_t ce = (int32_t)xr[c] - mean;
+        vs += (uint64_t)((uint32_t)ce * (uint32_t)ce);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) vs += __shfl_xor_sync(0xffffffffu, vs, o);
+    int64_t var;
+    switch (d) {
+    case 384: var = norm_reduce64<384>((int64_t)vs); break;
+    case 512: var = norm_reduce64<512>((int64_t)vs); break;
+    case 768: var = norm_reduce64<768>((int64_t)vs); break;
+    case 1024: var = norm_reduce64<1024>((int64_t)vs); break;
+    default: var = norm_reduce64<1280>((int64_t)vs); break;
+    }
+    if (lane == 0) {
+        mean_o[row] = mean;
+        var_o[row] = var;
+    }
+}
+
+cudaError_t layernorm64_stats(const int16_t *x, int rows, int d, int32_t *mean, int64_t *var, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    ln64_stats_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(x, rows, d, mean, var);
     return cudaGetLastError();
 }
 

@@ -12,7 +12,9 @@ struct LnParams {
     int32_t ln_shift;      // int8 value
     uint32_t out_mult;     // u32
     uint32_t out_shift;    // (uint32)(int32)int8: negative -> >= 32 -> 0
-    uint32_t rsqrt_offset; // 13 (LayerNorm_int.offset)
+    uint32_t rsqrt_offset; // 13 (LayerNorm_int.offset); 15 for LayerNorm64
+    int32_t additional_offset = 0;  // LayerNorm64 normalise-shift offset (2)
+    int *overflow = nullptr;        // LayerNorm64: set to 1 when a variance does not fit INT32
 };
 
 struct GeluParams {
@@ -50,9 +52,12 @@ struct AttnArgs {
 };
 
 cudaError_t rowsum_i8(const int8_t *x, int64_t ldx, int M, int K, int32_t *out, cudaStream_t st);
+// l64: the LayerNorm64 variant (p.rsqrt_offset / additional_offset / overflow)
 cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, const int32_t *beta, const LnParams &p,
                         int8_t *y, int64_t ldy, int rows, int d, int32_t *rowsum_out, int32_t *rowsum_zero,
-                        cudaStream_t st);
+                        cudaStream_t st, bool l64 = false);
+// LayerNorm64 statistics (layernorm_scalar.cpp:230-297): mean int32, variance int64
+cudaError_t layernorm64_stats(const int16_t *x, int rows, int d, int32_t *mean, int64_t *var, cudaStream_t st);
 cudaError_t layernorm32_stats(const int16_t *x, int rows, int d, int32_t *mean, int32_t *var, int32_t *rs,
                               cudaStream_t st);
 cudaError_t fisr_vec(const int32_t *x, int32_t *y, int64_t n, uint32_t off, cudaStream_t st);

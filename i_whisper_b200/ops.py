@@ -152,7 +152,7 @@ def _ln_width(x):
     return d
 
 
-def layernorm32_cuda(input, weight, bias, ln_multiplier, ln_shift, out_multiplier, out_shift):
+def layernorm32_cuda(input, weight, bias, ln_multiplier, ln_shift, out_multiplier, out_shift, _entry="iw_layernorm32"):
     """``_C.layernorm32_simd`` (layernorm_scalar.cpp:464-624, offset 13)."""
     _chk(input, "input", "int16"); _chk(weight, "weight", "int8")
     if input.dim() < 1:
@@ -167,7 +167,7 @@ def layernorm32_cuda(input, weight, bias, ln_multiplier, ln_shift, out_multiplie
         if bias.dim() != 1 or bias.numel() != d:
             raise RuntimeError(f"bias.numel() must equal input.size(-1), got {bias.numel()} expected {d}")
     y = torch.empty_like(input, dtype=torch.int8)
-    _lib.call("iw_layernorm32", input.data_ptr(), weight.data_ptr(), _p(bias), _scalar(ln_multiplier, "ln_multiplier"),
+    _lib.call(_entry, input.data_ptr(), weight.data_ptr(), _p(bias), _scalar(ln_multiplier, "ln_multiplier"),
               _scalar(ln_shift, "ln_shift"), _scalar(out_multiplier, "out_multiplier"), _scalar(out_shift, "out_shift"),
               y.data_ptr(), input.numel() // d, d, _stream())
     return y
@@ -183,6 +183,26 @@ def layernorm32_stats_cuda(input) -> Tuple[torch.Tensor, torch.Tensor, torch.Ten
     _lib.call("iw_layernorm32_stats", input.data_ptr(), mean.data_ptr(), var.data_ptr(), rs.data_ptr(), rows, d,
               _stream())
     return mean, var, rs
+
+
+def layernorm64_cuda(input, weight, bias, ln_multiplier, ln_shift, out_multiplier, out_shift):
+    """``_C.layernorm64_simd`` (layernorm_scalar.cpp:626-825; rsqrt offset 15,
+    normalise-shift offset 2 as layernorm_torch.cpp:446-460). OverflowError
+    when a row's variance does not fit INT32, as the reference."""
+    return layernorm32_cuda(input, weight, bias, ln_multiplier, ln_shift, out_multiplier, out_shift,
+                            _entry="iw_layernorm64")
+
+
+def layernorm64_stats_cuda(input) -> Tuple[torch.Tensor, torch.Tensor]:
+    """``_C.layernorm64_stats_simd`` (layernorm_scalar.cpp:230-297): mean
+    int32 and variance int64 per row."""
+    _chk(input, "input", "int16")
+    d = _ln_width(input)
+    rows = input.numel() // d
+    mean = torch.empty(rows, dtype=torch.int32, device=input.device)
+    var = torch.empty(rows, dtype=torch.int64, device=input.device)
+    _lib.call("iw_layernorm64_stats", input.data_ptr(), mean.data_ptr(), var.data_ptr(), rows, d, _stream())
+    return mean, var
 
 
 def layernorm32_rsqrt_cuda(input):

@@ -36,13 +36,15 @@ extern "C" {
 #define IW_EVALUE (-2)    /* value error (std::invalid_argument)            */
 #define IW_ECUDA (-3)     /* CUDA runtime error                             */
 #define IW_EDEVICE (-4)   /* device-side wait gave up (see iw_device_status) */
+#define IW_EOVERFLOW (-5) /* overflow (std::overflow_error)                 */
 
 /* Message of the last failed call on this thread ("" if none). */
 const char *iw_last_error(void);
 /* ABI version of this library. */
 int iw_abi_version(void);
 /* Synchronises the device, returns the device status word in *status
- * (bit 0: a bounded in-kernel wait timed out) and clears it if `clear`. */
+ * (bit 0: a bounded in-kernel wait timed out; bit 1: a LayerNorm64
+ * variance did not fit INT32 in iw_layernorm64_ex) and clears it if `clear`. */
 int iw_device_status(uint32_t *status, int clear);
 
 /* linear8_{scalar,simd} -- linear8_scalar.cpp:30-84; pybind.cpp:51-70.
@@ -86,6 +88,20 @@ int iw_layernorm32(const int16_t *x, const int8_t *weight, const int32_t *bias, 
  * pybind.cpp:185-194. mean/variance/renorm_shift [rows] int32. */
 int iw_layernorm32_stats(const int16_t *x, int32_t *mean, int32_t *variance, int32_t *renorm_shift, int64_t rows,
                          int64_t d, void *stream);
+
+/* layernorm64_{scalar,simd} -- layernorm_scalar.cpp:626-825;
+ * pybind.cpp:163-178 (LayerNorm_int backend "scalar64"/"simd64",
+ * model_int.py:252-287). Arguments as iw_layernorm32; rsqrt offset 15 and
+ * normalise-shift offset 2 as fixed by layernorm_torch.cpp:446-460.
+ * Synchronises; IW_EOVERFLOW when a row's int64 variance does not fit INT32
+ * (std::overflow_error in the reference), the output then undefined. */
+int iw_layernorm64(const int16_t *x, const int8_t *weight, const int32_t *bias, uint8_t ln_multiplier,
+                   int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y, int64_t rows, int64_t d,
+                   void *stream);
+
+/* layernorm64_stats_{scalar,simd} -- layernorm_scalar.cpp:230-297;
+ * pybind.cpp:153-162. mean [rows] int32, variance [rows] int64. */
+int iw_layernorm64_stats(const int16_t *x, int32_t *mean, int64_t *variance, int64_t rows, int64_t d, void *stream);
 
 /* layernorm32_rsqrt_scalar -- layernorm_scalar.cpp:383-437 (offset 13);
  * pybind.cpp:195-200. Synchronises to check that every input is >= 0. */
@@ -295,6 +311,12 @@ int iw_shift_exp_table(int32_t frac_bits, uint8_t *table, void *stream);
  * int8 output (rowsum_out) and zeroes rowsum_zero[rows] for a later
  * accumulating epilogue. */
 int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
+                      uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
+                      int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream);
+
+/* iw_layernorm32_ex for LayerNorm64 (no synchronisation: a variance that
+ * does not fit INT32 sets bit 1 of the iw_device_status word). */
+int iw_layernorm64_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
                       uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
                       int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream);
 

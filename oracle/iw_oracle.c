@@ -317,6 +317,82 @@ int iwo_layernorm32(const int16_t *x, const int8_t *gamma, const int32_t *beta,
     return 0;
 }
 
+/* ---- LayerNorm64 (research variant) ---------------------------------------- */
+/* layernorm_scalar.cpp:58-90 -- the 64-bit width division of the unshifted
+ * variance sum. */
+static inline int norm_reduce64(int64_t x, int64_t d, int64_t *out) {
+    switch (d) {
+    case 384: *out = (x + (x >> 2) + (x >> 3)) >> 9; return 0;
+    case 512: *out = x >> 9; return 0;
+    case 768: *out = (x + (x >> 2) + (x >> 3)) >> 10; return 0;
+    case 1024: *out = x >> 10; return 0;
+    case 1280: *out = (x + (x >> 1)) >> 11; return 0;
+    default: return -1;
+    }
+}
+
+/* layernorm_scalar.cpp:230-297 -- the LayerNorm32 mean, then the full
+ * int64 sum of centred squares (no renorm pre-shift), width-divided. */
+static int ln64_row_stats(const int16_t *r, int64_t d, int32_t *mean_out, int64_t *var_out) {
+    uint32_t s = 0;
+    for (int64_t c = 0; c < d; ++c) s += (uint32_t)(int32_t)r[c];
+    int32_t mean;
+    if (norm_reduce((int32_t)s, d, &mean)) return -1;
+    int64_t vs = 0;
+    for (int64_t c = 0; c < d; ++c) {
+        const int64_t ce = (int64_t)r[c] - (int64_t)mean;
+        vs += ce * ce;
+    }
+    int64_t var;
+    norm_reduce64(vs, d, &var);
+    *mean_out = mean;
+    *var_out = var;
+    return 0;
+}
+
+int iwo_layernorm64_stats(const int16_t *x, int32_t *mean, int64_t *var,
+                          int64_t rows, int64_t d) {
+    int64_t dummy;
+    if (norm_reduce64(0, d, &dummy)) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) ln64_row_stats(x + r * d, d, &mean[r], &var[r]);
+    return 0;
+}
+
+/* layernorm_scalar.cpp:626-825 -- FISR of the int64 variance (which must fit
+ * INT32) with rsqrt_offset, normalise shift ln_shift + additional_offset
+ * (no renorm term), otherwise the LayerNorm32 element chain. */
+int iwo_layernorm64(const int16_t *x, const int8_t *gamma, const int32_t *beta,
+                    uint8_t ln_mult, int8_t ln_shift, uint32_t out_mult,
+                    int8_t out_shift, uint32_t rsqrt_offset,
+                    int32_t additional_offset, int8_t *y, int64_t rows,
+                    int64_t d) {
+    int64_t dummy;
+    if (norm_reduce64(0, d, &dummy)) return -1;
+    for (int64_t r = 0; r < rows; ++r) {  /* rows in order: the first overflow stops, as in the reference */
+        const int16_t *xr = x + r * d;
+        int8_t *yr = y + r * d;
+        int32_t mean;
+        int64_t var64;
+        ln64_row_stats(xr, d, &mean, &var64);
+        if (var64 < 0 || var64 > (int64_t)INT32_MAX) return -2;
+        const int32_t inv = iwo_fisr((int32_t)var64, rsqrt_offset);
+        const int32_t nshift = (int32_t)ln_shift + additional_offset;
+        for (int64_t c = 0; c < d; ++c) {
+            int32_t v = wmul((int32_t)xr[c] - mean, inv);
+            v = wmul(v, (int32_t)ln_mult);
+            v = iwo_rounding_rshift(v, (uint32_t)nshift);
+            v = clampi(v, -16383, 16383);
+            v = wmul(v, (int32_t)gamma[c]);
+            if (beta) v = wadd(v, beta[c]);
+            v = iwo_mulh(v, out_mult);
+            v = iwo_rounding_rshift(v, (uint32_t)(int32_t)out_shift);
+            yr[c] = (int8_t)clampi(v, -127, 127);
+        }
+    }
+    return 0;
+}
+
 /* ---- GeLU ----------------------------------------------------------------- */
 /* gelu_scalar.cpp:10-181 -- LUT index = rrs(x*mi, clamp(si,0,32)) + 8,
  * clamped to [0,15]; y = rrs(x*lut[idx]*mo, clamp(so,0,32)), clamp +-127.

@@ -55,6 +55,17 @@ int iwo_layernorm32(const int16_t *x, const int8_t *gamma, const int32_t *beta,
 int iwo_layernorm32_stats(const int16_t *x, int32_t *mean, int32_t *var,
                           int32_t *renorm_shift, int64_t rows, int64_t d);
 
+/* LayerNorm64 research variant (layernorm_scalar.cpp:230-297, 626-825):
+ * returns -1 on an unsupported width, -2 when a row's variance does not fit
+ * INT32 (the reference throws std::overflow_error). */
+int iwo_layernorm64(const int16_t *x, const int8_t *gamma, const int32_t *beta,
+                    uint8_t ln_mult, int8_t ln_shift, uint32_t out_mult,
+                    int8_t out_shift, uint32_t rsqrt_offset,
+                    int32_t additional_offset, int8_t *y, int64_t rows,
+                    int64_t d);
+int iwo_layernorm64_stats(const int16_t *x, int32_t *mean, int64_t *var,
+                          int64_t rows, int64_t d);
+
 /* GeLU (gelu_scalar.cpp) */
 void iwo_gelu(const int8_t *x, const uint8_t *lut, const uint8_t *mi,
               const int8_t *si, const uint8_t *mo, const int8_t *so,

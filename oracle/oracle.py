@@ -44,6 +44,9 @@ _SIGS = {
     "residual15": ([_P, _P, C.c_uint16, _P, _I64], None),
     "layernorm32": ([_P, _P, _P, C.c_uint8, C.c_int8, C.c_uint32, C.c_int8, C.c_uint32, _P, _I64, _I64], C.c_int),
     "layernorm32_stats": ([_P, _P, _P, _P, _I64, _I64], C.c_int),
+    "layernorm64": ([_P, _P, _P, C.c_uint8, C.c_int8, C.c_uint32, C.c_int8, C.c_uint32, C.c_int32, _P, _I64, _I64],
+                    C.c_int),
+    "layernorm64_stats": ([_P, _P, _P, _I64, _I64], C.c_int),
     "fisr_vec": ([_P, _P, _I64, C.c_uint32], None),
     "gelu": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64], None),
     "qk": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64], None),
@@ -134,6 +137,39 @@ class OracleLib:
         if rc != 0:
             raise ValueError(f"unsupported LayerNorm hidden size: {d}")
         return y
+
+    def layernorm64(self, x, gamma, beta, ln_m, ln_s, out_m, out_s, rsqrt_offset=15, additional_offset=2):
+        """LayerNorm64 (layernorm_torch.cpp:446-460 fixes rsqrt_offset 15 and
+        additional_offset 2); OverflowError when a row's variance does not
+        fit INT32, as the reference."""
+        x = _c(x, np.int16); d = x.shape[-1]
+        y = np.empty(x.shape, np.int8)
+        rc = self.fn["layernorm64"](_ptr(x), _ptr(_c(gamma, np.int8)), _ptr(_c(beta, np.int32)),
+                                    int(np.asarray(ln_m).reshape(-1)[0]), int(np.asarray(ln_s).reshape(-1)[0]),
+                                    int(np.asarray(out_m).reshape(-1)[0]), int(np.asarray(out_s).reshape(-1)[0]),
+                                    rsqrt_offset, additional_offset, _ptr(y), x.size // d, d)
+        if rc == -2:
+            raise OverflowError("LayerNorm64 variance does not fit INT32")
+        if rc != 0:
+            raise ValueError(f"unsupported LayerNorm hidden size: {d}")
+        return y
+
+    def layernorm64_stats(self, x):
+        x = _c(x, np.int16); d = x.shape[-1]; rows = x.size // d
+        mean = np.empty(rows, np.int32); var = np.empty(rows, np.int64)
+        rc = self.fn["layernorm64_stats"](_ptr(x), _ptr(mean), _ptr(var), rows, d)
+        if rc != 0:
+            raise ValueError(f"unsupported LayerNorm hidden size: {d}")
+        return mean, var
+
+    def with_layernorm(self, variant: str) -> "OracleLib":
+        """A view of this library whose model dataflow uses LayerNorm32 ("32",
+        the reference default) or the LayerNorm64 research variant ("64",
+        backend "scalar64" of LayerNorm_int, model_int.py:252-287)."""
+        import copy
+        v = copy.copy(self)
+        v.ln_variant = variant
+        return v
 
     def layernorm32_stats(self, x):
         x = _c(x, np.int16); d = x.shape[-1]; rows = x.size // d
@@ -278,6 +314,10 @@ def _lin32(L, P, pre, x):
 
 
 def _ln(L, P, pre, x):
+    if getattr(L, "ln_variant", "32") == "64":
+        return L.layernorm64(x, P[pre + ".weight"], P.get(pre + ".bias"), P[pre + ".ln_req_multiplier"],
+                             P[pre + ".ln_req_shiftmount"], P[pre + ".out_req_multiplier"],
+                             P[pre + ".out_req_shiftmount"])
     return L.layernorm32(x, P[pre + ".weight"], P.get(pre + ".bias"), P[pre + ".ln_req_multiplier"],
                          P[pre + ".ln_req_shiftmount"], P[pre + ".out_req_multiplier"],
                          P[pre + ".out_req_shiftmount"], 13)
@@ -346,10 +386,11 @@ def block_forward(L, P, pre, x, n_head, xa=None, mask=None, cache=None, trace=No
     return x
 
 
-def encoder_forward(P, dims: Dims, mel_i8: np.ndarray, kind="port", trace=None) -> np.ndarray:
+def encoder_forward(P, dims: Dims, mel_i8: np.ndarray, kind="port", trace=None, layernorm="32") -> np.ndarray:
     """AudioEncoder_int.forward (model_int.py:1260-1316) on an INT8 mel
-    [B,n_mels,2*n_audio_ctx] -> INT8 [B,n_audio_ctx,d]."""
-    L = lib(kind)
+    [B,n_mels,2*n_audio_ctx] -> INT8 [B,n_audio_ctx,d]; layernorm "64" puts
+    every LayerNorm_int on its LayerNorm64 backend."""
+    L = lib(kind).with_layernorm(layernorm)
     e = "encoder"
     x = L.conv1d(mel_i8, P[e + ".conv1.weight"], P.get(e + ".conv1.bias"), P[e + ".conv1.req_multiplier"],
                  P[e + ".conv1.req_shiftmount"], 1, 1)
@@ -369,11 +410,11 @@ def encoder_forward(P, dims: Dims, mel_i8: np.ndarray, kind="port", trace=None) 
 
 
 def decoder_forward(P, dims: Dims, tokens: np.ndarray, xa: np.ndarray, caches: List[dict], offset: int,
-                    kind="port") -> np.ndarray:
+                    kind="port", layernorm="32") -> np.ndarray:
     """TextDecoder_int.forward (model_int.py:1398-1484) with the KV cache
     hooks of Whisper_int.install_kv_cache_hooks (:1587-1618): INT8 logits
     [B,T,V] (before the float dequantisation)."""
-    L = lib(kind)
+    L = lib(kind).with_layernorm(layernorm)
     d = "decoder"
     emb = P[d + ".token_embedding.weight"][tokens]
     pe = P[d + ".positional_embedding"][offset:offset + tokens.shape[-1]]
@@ -435,7 +476,7 @@ def apply_filters_torch(logits, tokens, tk: DecodeTokens, sample_begin: int):
 
 
 def greedy_decode(P, dims: Dims, xa: np.ndarray, tk: DecodeTokens, sample_len: int, kind="port",
-                  stop_when_done=True) -> np.ndarray:
+                  stop_when_done=True, layernorm="32") -> np.ndarray:
     """DecodingTask._main_loop with GreedyDecoder (decoding.py:684-712,
     280-296): returns the token matrix [B, len(sot_sequence)+steps]."""
     import torch
@@ -447,7 +488,7 @@ def greedy_decode(P, dims: Dims, xa: np.ndarray, tk: DecodeTokens, sample_len: i
     offset = 0
     for i in range(sample_len):
         inp = tokens.numpy() if i == 0 else tokens[:, -1:].numpy()
-        logits8 = decoder_forward(P, dims, inp, xa, caches, offset, kind)
+        logits8 = decoder_forward(P, dims, inp, xa, caches, offset, kind, layernorm)
         offset += inp.shape[1]
         logits = torch.from_numpy(logits8[:, -1].astype(np.float32)).div(torch.tensor([alpha], dtype=torch.float32))
         apply_filters_torch(logits, tokens, tk, sample_begin)

@@ -58,6 +58,25 @@ int iwr_layernorm32_stats(const int16_t *x, int32_t *mean, int32_t *var, int32_t
     }
     return 0;
 }
+int iwr_layernorm64(const int16_t *x, const int8_t *g, const int32_t *b, uint8_t lm, int8_t ls,
+                    uint32_t om, int8_t os, uint32_t off, int32_t add, int8_t *y, int64_t rows, int64_t d) {
+    try {
+        layernorm64_scalar(x, g, b, lm, ls, om, os, off, add, y, rows, d, b != nullptr);
+    } catch (const std::overflow_error &) {
+        return -2;
+    } catch (const std::exception &) {
+        return -1;
+    }
+    return 0;
+}
+int iwr_layernorm64_stats(const int16_t *x, int32_t *mean, int64_t *var, int64_t rows, int64_t d) {
+    try {
+        layernorm64_stats_scalar(x, mean, var, rows, d);
+    } catch (const std::exception &) {
+        return -1;
+    }
+    return 0;
+}
 void iwr_fisr_vec(const int32_t *x, int32_t *y, int64_t n, uint32_t off) {
     layernorm32_rsqrt_scalar(x, y, n, off);
 }

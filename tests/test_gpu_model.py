@@ -77,6 +77,25 @@ def test_device_status_clean_after_model():
     assert _lib.device_status(clear=True) == 0
 
 
+def test_model_layernorm64_matches_oracle():
+    """Every LayerNorm_int on its LayerNorm64 backend: encoder output and
+    greedy tokens against the oracle dataflow with the same variant."""
+    from i_whisper_b200 import _lib
+    from i_whisper_b200.model import WhisperIntB200
+    dims = ModelDims(80, 1500, 512, 8, 2, 51865, 448, 512, 8, 2)
+    sd = synthetic_state_dict(dims, 11)
+    mel = synthetic_mel_batch(dims.n_mels, [4, 5], float(sd["encoder.input_alpha"][0]))
+    odims = O.Dims(**dims.__dict__)
+    xa_ref = O.encoder_forward(sd, odims, mel, layernorm="64")
+    model = WhisperIntB200(dims, sd, layernorm="64")
+    xa = model.encoder(torch.from_numpy(mel).cuda())
+    assert np.array_equal(xa.cpu().numpy(), xa_ref)
+    ref = O.greedy_decode(sd, odims, xa_ref, decode_spec(dims.n_vocab), 6, stop_when_done=False, layernorm="64")
+    toks = model.decode(xa, model._enc_ws[2]["rs_xa"], 6, use_graph=True)
+    assert toks.cpu().numpy().tolist() == ref.tolist()
+    assert _lib.device_status(clear=True) == 0
+
+
 def test_encode_batches_pipelined():
     """The host-buffer streaming API (uploads and downloads overlapping the
     neighbouring batches' compute) returns, batch for batch, what the

@@ -119,6 +119,46 @@ def test_layernorm32(ops, L, d, rows):
         assert np.array_equal(host(b), a)
 
 
+@pytest.mark.parametrize("d", [384, 768, 1280])
+def test_layernorm32_full_range(ops, L, d):
+    """Rows beyond INT15, where the reference's int32 centred squares wrap."""
+    rng = np.random.default_rng(d)
+    x = rng.integers(-32768, 32768, (6, d), dtype=np.int16)
+    x[1, : d // 2], x[1, d // 2:] = 32767, -32768
+    x[2, :3], x[2, 3:] = 32767, -32768
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    ref = L.layernorm32(x, g, be, 200, 5, 2 ** 30, 12)
+    got = ops.layernorm32_cuda(dev(x), dev(g), dev(be), 200, 5, 2 ** 30, 12)
+    assert np.array_equal(host(got), ref)
+    for a, b in zip(L.layernorm32_stats(x), ops.layernorm32_stats_cuda(dev(x))):
+        assert np.array_equal(host(b), a)
+
+
+@pytest.mark.parametrize("d", [384, 512, 768, 1024, 1280])
+@pytest.mark.parametrize("full", [False, True])
+def test_layernorm64(ops, L, d, full):
+    """LayerNorm64 research variant (backend scalar64/simd64) against the
+    oracle restatement of layernorm64_scalar."""
+    rng = np.random.default_rng(d * 3 + full)
+    lo = -32768 if full else -16383
+    x = rng.integers(lo, -lo, (37, d), dtype=np.int16)
+    x[0] = x[0] // 64
+    if full:
+        x[1, : d // 2], x[1, d // 2:] = 32767, -32768
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    for (lm, ls, om, os) in [(200, 5, 2 ** 31 + 12345, 7), (255, 0, 0xFFFFFFFF, 0), (37, -2, 2 ** 30, -1)]:
+        ref = L.layernorm64(x, g, be, lm, ls, om, os)
+        got = ops.layernorm64_cuda(dev(x), dev(g), dev(be), lm, ls, om, os)
+        assert np.array_equal(host(got), ref), (lm, ls, om, os)
+    ref = L.layernorm64(x, g, None, 120, 7, 2 ** 31, 9)
+    got = ops.layernorm64_cuda(dev(x), dev(g), None, 120, 7, 2 ** 31, 9)
+    assert np.array_equal(host(got), ref)
+    for a, b in zip(L.layernorm64_stats(x), ops.layernorm64_stats_cuda(dev(x))):
+        assert np.array_equal(host(b), a)
+
+
 def test_layernorm32_zero_rows(ops, L):
     x = np.zeros((4, 512), np.int16)
     g = np.ones(512, np.int8)

@@ -71,6 +71,39 @@ def test_layernorm(P, R, d):
     assert eq(P.layernorm32_stats(x), R.layernorm32_stats(x))
 
 
+@pytest.mark.parametrize("d", [384, 512, 768, 1024, 1280])
+def test_layernorm_full_int16_range(P, R, d):
+    """Rows beyond INT15: the reference squares the centred values in int32
+    (wrapping past 46340) before the renorm shift."""
+    rng = np.random.default_rng(100 + d)
+    x = rng.integers(-32768, 32768, (6, d), dtype=np.int16)
+    x[1, : d // 2], x[1, d // 2:] = 32767, -32768
+    x[2, :3], x[2, 3:] = 32767, -32768
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    assert eq(P.layernorm32(x, g, be, 200, 5, 2 ** 30, 12), R.layernorm32(x, g, be, 200, 5, 2 ** 30, 12))
+    assert eq(P.layernorm32_stats(x), R.layernorm32_stats(x))
+
+
+@pytest.mark.parametrize("d", [384, 512, 768, 1024, 1280])
+def test_layernorm64(P, R, d):
+    """The LayerNorm64 research variant (layernorm_scalar.cpp:230-297,
+    626-825) with the torch wrapper's rsqrt offset 15 and offset 2."""
+    rng = np.random.default_rng(200 + d)
+    x = rng.integers(-32768, 32768, (9, d), dtype=np.int16)
+    x[1] = 0
+    x[2] = x[2] // 256
+    x[3, : d // 2], x[3, d // 2:] = 32767, -32768
+    x[4] = rng.integers(-16383, 16384, d)
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    for lm, ls, om, os_ in [(200, 5, 2 ** 31 + 12345, 7), (255, 0, 0xFFFFFFFF, 0), (1, 20, 123456789, 31),
+                            (37, -2, 2 ** 30, -1), (128, 7, 2 ** 31, 40)]:
+        assert eq(P.layernorm64(x, g, be, lm, ls, om, os_), R.layernorm64(x, g, be, lm, ls, om, os_))
+        assert eq(P.layernorm64(x, g, None, lm, ls, om, os_), R.layernorm64(x, g, None, lm, ls, om, os_))
+    assert eq(P.layernorm64_stats(x), R.layernorm64_stats(x))
+
+
 def test_layernorm_bad_width(P):
     with pytest.raises(ValueError):
         P.layernorm32(np.zeros((1, 100), np.int16), np.zeros(100, np.int8), None, 1, 0, 1, 0)
