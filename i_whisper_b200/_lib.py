@@ -57,6 +57,7 @@ SIGNATURES = {
     "iw_kv_append": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "iw_greedy_step": [_P, _I64, _P],
     "iw_add_i32": [_P, _I32, _P],
+    "iw_log_mel_int8": [_P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P],
     "iw_gelu_table": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
     "iw_shift_exp_table": [_I32, _P, _P],
     "iw_linear8_noalloc": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],

@@ -625,6 +625,21 @@ int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream) {
     return cuda_check(iw::greedy_step(g, (int)B, S(stream)), "iw_greedy_step");
 }
 
+int iw_log_mel_int8(const float *audio, int64_t B, int64_t n_samples, int64_t lda, const float *filters,
+                    int64_t n_mels, float input_alpha, int8_t *out, void *stream) {
+    if (B < 0 || n_samples <= 256 || n_samples > INT32_MAX || lda < n_samples || n_mels <= 0 || n_mels > 128)
+        return fail(IW_EINVAL, "iw_log_mel_int8: invalid shape");
+    if (B == 0) return IW_OK;
+    cudaStream_t st = S(stream);
+    const int64_t frames = n_samples / 160;
+    Scratch work(st), wmax(st);
+    if (int r = cuda_check(work.alloc((size_t)(B * n_mels * frames) * sizeof(float)), "iw_log_mel_int8")) return r;
+    if (int r = cuda_check(wmax.alloc((size_t)B * sizeof(int32_t)), "iw_log_mel_int8")) return r;
+    return cuda_check(iw::log_mel_int8(audio, (int)B, (int)n_samples, lda, filters, (int)n_mels, input_alpha,
+                                       (float *)work.p, (int32_t *)wmax.p, out, st),
+                      "iw_log_mel_int8");
+}
+
 int iw_add_i32(int32_t *p, int32_t v, void *stream) {
     return cuda_check(iw::add_i32(p, v, S(stream)), "iw_add_i32");
 }

@@ -5,5 +5,6 @@
 #include "gemm_cm.cu"
 #include "kernels.cu"
 #include "attn_tc.cu"
+#include "frontend.cu"
 #include "capi.cu"
 #include "noalloc.cu"

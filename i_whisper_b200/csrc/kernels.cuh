@@ -108,6 +108,13 @@ struct GreedyArgs {
     int64_t *next;             // [B] next token (also fed to the embedding gather)
 };
 cudaError_t greedy_step(const GreedyArgs &g, int B, cudaStream_t st);
+
+// Log-mel + INT8 quantisation of B windows of n_samples float audio (row
+// stride lda): out [B, n_mels, n_samples/160]; filters [n_mels, 257] on the
+// device; work [B, n_mels, n_samples/160] floats and wmax [B] ints.
+cudaError_t log_mel_int8(const float *audio, int B, int n_samples, int64_t lda, const float *filters, int n_mels,
+                         float alpha, float *work, int32_t *wmax, int8_t *out, cudaStream_t st);
+size_t logmel_smem_bytes(int n_mels);
 cudaError_t add_i32(int32_t *p, int32_t v, cudaStream_t st);
 cudaError_t qk_requant_rowmax(const int8_t *q, const int8_t *k, const uint8_t *mask, int16_t *qk, int16_t *rmax1,
                               int B, int H, int Tq, int Tk, int D, uint8_t mult, int32_t shift, cudaStream_t st);

@@ -193,9 +193,23 @@ def bench_cross_attention(B: int, H: int, T: int, reps: int, seed: int) -> dict:
             "frac": round(gbs / hbm, 4), "peak_gbs": hbm, "peak_source": src, "algorithmic_bytes": nbytes}
 
 
+def bench_frontend(B: int, n_mels: int, reps: int, seed: int) -> dict:
+    """GPU log-mel + INT8 quantisation of B windows of 30 s audio."""
+    from .frontend import log_mel_int8_cuda
+    g = torch.Generator().manual_seed(seed)
+    audio = (torch.randn(B, 480000, generator=g) * 0.2).cuda()
+    ms = _time(lambda: log_mel_int8_cuda(audio, n_mels, 100.0), reps)
+    hbm, src = hbm_peak()
+    nbytes = B * (480000 * 4 + n_mels * 3000)
+    return {"op": "frontend", "B": B, "n_mels": n_mels, "ms": round(ms, 4), "windows_per_s": round(B / ms * 1e3, 1),
+            "gbs": round(nbytes / ms / 1e6, 1), "frac": round(nbytes / ms / 1e6 / hbm, 4), "peak_gbs": hbm,
+            "peak_source": src}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    p.add_argument("op", choices=["gemm", "layernorm", "attention", "cross_attention"])
+    p.add_argument("op", choices=["gemm", "layernorm", "attention", "cross_attention", "frontend"])
+    p.add_argument("--n-mels", type=int, default=80)
     p.add_argument("--M", type=int, default=12000)
     p.add_argument("--K", type=int, default=1024)
     p.add_argument("--N", type=int, default=4096)
@@ -221,6 +235,8 @@ def main(argv=None):
         r = bench_layernorm(a.rows, a.d, a.reps, a.seed)
     elif a.op == "attention":
         r = bench_attention(a.B, a.H, a.T, a.reps, a.seed)
+    elif a.op == "frontend":
+        r = bench_frontend(a.B, a.n_mels, a.reps, a.seed)
     else:
         r = bench_cross_attention(a.B, a.H, a.T, a.reps, a.seed)
     if _lib.device_status(clear=True) != 0:

@@ -7,18 +7,18 @@ amplitudes and phases, plus Gaussian noise of sigma 0.05).
 the float log-mel of i_whisper/audio.py:216-265 (n_fft 512, hop 160, Hann
 window, power spectrum without the last frame, Slaney mel filterbank,
 log10 clamped at max-8, /4+1) followed by the input quantisation of
-AudioEncoder_int.forward (model_int.py:1265-1267). The mel filterbank is
-the published Slaney construction (the reference gets it from librosa,
-which is not installed); frontend parity is therefore not claimed -- both
-the oracle and the GPU path consume the same INT8 bytes.
+AudioEncoder_int.forward (model_int.py:1265-1267), in float64 numpy. The
+mel filterbank is the published Slaney construction (the reference gets it
+from librosa, which is not installed). The GPU frontend (frontend.py)
+computes the same in float32; the benchmark feeds this INT8 mel so the
+oracle and the GPU encoder consume the same bytes.
 """
 from __future__ import annotations
 
 import numpy as np
 
-SAMPLE_RATE = 16000
-N_FFT = 512
-HOP = 160
+from .frontend import HOP, N_FFT, SAMPLE_RATE, mel_filterbank
+
 N_SAMPLES = 30 * SAMPLE_RATE
 
 
@@ -33,42 +33,6 @@ def synthetic_audio(seed: int) -> np.ndarray:
         x += a * np.sin(2 * np.pi * f * t + ph)
     x += rng.normal(0.0, 0.05, N_SAMPLES)
     return x.astype(np.float32)
-
-
-def _hz_to_mel(f):
-    f = np.asarray(f, np.float64)
-    f_sp = 200.0 / 3
-    mels = f / f_sp
-    min_log_hz = 1000.0
-    min_log_mel = min_log_hz / f_sp
-    logstep = np.log(6.4) / 27.0
-    return np.where(f >= min_log_hz, min_log_mel + np.log(np.maximum(f, 1e-10) / min_log_hz) / logstep, mels)
-
-
-def _mel_to_hz(m):
-    m = np.asarray(m, np.float64)
-    f_sp = 200.0 / 3
-    freqs = f_sp * m
-    min_log_hz = 1000.0
-    min_log_mel = min_log_hz / f_sp
-    logstep = np.log(6.4) / 27.0
-    return np.where(m >= min_log_mel, min_log_hz * np.exp(logstep * (m - min_log_mel)), freqs)
-
-
-def mel_filterbank(n_mels: int, n_fft: int = N_FFT, sr: int = SAMPLE_RATE) -> np.ndarray:
-    """Slaney-scale triangular filters with area normalisation."""
-    fft_freqs = np.linspace(0, sr / 2, 1 + n_fft // 2)
-    mel_pts = np.linspace(_hz_to_mel(0.0), _hz_to_mel(sr / 2), n_mels + 2)
-    hz = _mel_to_hz(mel_pts)
-    fdiff = np.diff(hz)
-    ramps = hz[:, None] - fft_freqs[None, :]
-    w = np.zeros((n_mels, len(fft_freqs)))
-    for i in range(n_mels):
-        lower = -ramps[i] / fdiff[i]
-        upper = ramps[i + 2] / fdiff[i + 1]
-        w[i] = np.maximum(0, np.minimum(lower, upper))
-    w *= (2.0 / (hz[2:n_mels + 2] - hz[:n_mels]))[:, None]
-    return w.astype(np.float32)
 
 
 def log_mel(audio: np.ndarray, n_mels: int) -> np.ndarray:

@@ -357,6 +357,19 @@ typedef struct iw_greedy_desc {
  * (IW_EINVAL otherwise). */
 int iw_greedy_step(const iw_greedy_desc *d, int64_t B, void *stream);
 
+/* log_mel_spectrogram (i_whisper/audio.py:216-265) followed by the input
+ * quantisation of AudioEncoder_int.forward (model_int.py:1265-1267) for B
+ * windows of float32 16 kHz audio [B, n_samples] (row stride lda floats,
+ * n_samples > 256): out [B, n_mels, n_samples/160] int8 =
+ * clamp(round((max(lg, max_window(lg) - 8)/4 + 1) * input_alpha), +-127)
+ * with lg = log10(max(filters @ |STFT|^2, 1e-10)), STFT n_fft 512, hop 160,
+ * periodic Hann window, reflect padding, last frame dropped. filters is the
+ * [n_mels, 257] float32 mel filterbank on the device (n_mels <= 128). The
+ * max is taken per window. Float32 arithmetic: results agree with the
+ * reference within one INT8 unit, not bit for bit. */
+int iw_log_mel_int8(const float *audio, int64_t B, int64_t n_samples, int64_t lda, const float *filters,
+                    int64_t n_mels, float input_alpha, int8_t *out, void *stream);
+
 /* *p += v on the device (advances device-side decode counters). */
 int iw_add_i32(int32_t *p, int32_t v, void *stream);
 

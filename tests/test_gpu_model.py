@@ -112,3 +112,18 @@ def test_encode_batches_pipelined():
     for m, o in zip(mels, outs):
         want = model.encoder(m.cuda()).cpu()
         assert torch.equal(o, want)
+
+
+def test_encoder_from_audio():
+    """Raw audio -> GPU frontend -> encoder equals the encoder on the INT8 mel
+    the same frontend produces (the frontend is checked separately)."""
+    from i_whisper_b200.frontend import log_mel_int8_cuda
+    from i_whisper_b200.model import WhisperIntB200
+    from i_whisper_b200.synthetic import synthetic_audio
+    dims = ModelDims(80, 1500, 384, 6, 1, 51865, 448, 384, 6, 1)
+    sd = synthetic_state_dict(dims, 2)
+    model = WhisperIntB200(dims, sd)
+    audio = torch.from_numpy(np.stack([synthetic_audio(s) for s in (3, 4)])).cuda()
+    got = model.encoder_from_audio(audio).clone()
+    mel = log_mel_int8_cuda(audio, 80, float(sd["encoder.input_alpha"][0]))
+    assert torch.equal(got, model.encoder(mel))

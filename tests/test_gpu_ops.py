@@ -592,3 +592,21 @@ def test_linear8_kv_cache_out(ops, L, B, T, H, pos, dev_pos):
     want_v[:, :, pos:pos + T] = vv
     assert np.array_equal(host(kc), want_k)
     assert np.array_equal(host(vc), want_v)
+
+
+@pytest.mark.parametrize("n_mels", [80, 128])
+def test_log_mel_int8_frontend(n_mels):
+    """GPU log-mel + INT8 quantisation against the float64 restatement of
+    audio.py:216-265 (itself checked against the reference's function):
+    float32 vs float64, so at most one INT8 unit apart, almost always equal."""
+    from i_whisper_b200.frontend import log_mel_int8_cuda
+    from i_whisper_b200.synthetic import log_mel_int8, synthetic_audio
+    audio = np.stack([synthetic_audio(s) for s in (1, 2, 3)])
+    alpha = 100.0
+    want = np.stack([log_mel_int8(a, n_mels, alpha) for a in audio]).astype(np.int32)
+    got = host(log_mel_int8_cuda(dev(audio), n_mels, alpha)).astype(np.int32)
+    assert got.shape == want.shape == (3, n_mels, 3000)
+    d = np.abs(got - want)
+    assert d.max() <= 1 and (d == 0).mean() > 0.999
+    one = host(log_mel_int8_cuda(dev(audio[1]), n_mels, alpha)).astype(np.int32)
+    assert np.array_equal(one, got[1])  # a window's result does not depend on its batch
