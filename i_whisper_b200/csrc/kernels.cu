@@ -513,6 +513,19 @@ static constexpr int kAttnWarps = kAttnThreads / 32;
 static constexpr int kAttnU = 4;                   // 64-key groups in flight per lane
 static constexpr int kAttnKeysPerPass = kAttnThreads / 4;
 
+// 16-byte asynchronous global -> shared copy (L2 only); a thread waits for
+// its own copies with cp_async_wait<n> (all but the n most recent groups).
+IW_DEV void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+IW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+IW_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kAttnRing = 3;  // K chunks of kAttnU*64 keys: one computed, two in flight
+
 IW_DEV int4 ld_nc_v4(const int8_t *p) {
     int4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0, %1, %2, %3}, [%4];"
@@ -528,7 +541,10 @@ IW_DEV int32_t dp4a_us(uint32_t a, int32_t b, int32_t c) {
     return d;
 }
 
-template <int QB>
+// RING: K streams through a cp.async shared-memory ring (long key sequences,
+// where the scores pass is bound by load latency); otherwise direct loads,
+// which keep the shared-memory footprint (and so occupancy) of short ones.
+template <int QB, bool RING>
 __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     pdl_wait();
     pdl_launch();
@@ -539,7 +555,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     const int q0 = blockIdx.x * QB;
     const int nq = min(QB, Tq - q0);
     if (nq <= 0) return;
-    int16_t *s = reinterpret_cast<int16_t *>(smem);          // [QB][Tk]
+    constexpr int kChunk = kAttnU * kAttnKeysPerPass;        // keys per K chunk
+    int8_t *kring = reinterpret_cast<int8_t *>(smem);        // [kAttnRing][kChunk][64] when RING
+    int16_t *s = reinterpret_cast<int16_t *>(smem + (RING ? kAttnRing * kChunk * 64 : 0));  // [QB][Tk]
     uint8_t *pp = reinterpret_cast<uint8_t *>(s + QB * Tk);  // [QB][Tk]
     __shared__ int32_t red[QB][kAttnWarps];
     __shared__ int32_t rowv[QB][2];
@@ -565,13 +583,42 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     for (int r = 0; r < QB; ++r) lmax[r] = -32768;
     const uint32_t qsh = (uint32_t)(a.qk_shift > 0 ? a.qk_shift : 0);
     const int8_t *kb = a.k + (int64_t)b * a.k_bs + (int64_t)h * a.k_hs + 16 * sub;
-    for (int j0 = 0; j0 < Tk; j0 += kAttnU * kAttnKeysPerPass) {
-        int4 kk[kAttnU];
+    // With RING each thread copies exactly the 16-byte pieces it computes on,
+    // so it only waits for its own copies (no block barrier) and the loads in
+    // flight hold no registers.
+    const int nchunks = (Tk + kChunk - 1) / kChunk;
+    auto issue = [&](int c) {
+        if (!RING) return;
+        if (c < nchunks) {
 #pragma unroll
-        for (int u = 0; u < kAttnU; ++u) {
-            const int j = j0 + u * kAttnKeysPerPass + slot;
-            kk[u] = j < Tk ? ld_nc_v4(kb + (int64_t)j * a.ldk) : make_int4(0, 0, 0, 0);
+            for (int u = 0; u < kAttnU; ++u) {
+                const int jl = u * kAttnKeysPerPass + slot, j = c * kChunk + jl;
+                if (j < Tk) cp_async16(kring + ((c % kAttnRing) * kChunk + jl) * 64 + 16 * sub, kb + (int64_t)j * a.ldk);
+            }
         }
+        cp_async_commit();  // possibly empty: keeps the group count uniform
+    };
+    for (int c = 0; c < kAttnRing - 1; ++c) issue(c);
+    for (int c = 0; c < nchunks; ++c) {
+        const int j0 = c * kChunk;
+        int4 kk[kAttnU];
+        if constexpr (RING) {
+            cp_async_wait<kAttnRing - 2>();  // chunk c has landed
+#pragma unroll
+            for (int u = 0; u < kAttnU; ++u) {
+                const int jl = u * kAttnKeysPerPass + slot;
+                kk[u] = j0 + jl < Tk
+                            ? *reinterpret_cast<const int4 *>(kring + ((c % kAttnRing) * kChunk + jl) * 64 + 16 * sub)
+                            : make_int4(0, 0, 0, 0);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < kAttnU; ++u) {
+                const int j = j0 + u * kAttnKeysPerPass + slot;
+                kk[u] = j < Tk ? ld_nc_v4(kb + (int64_t)j * a.ldk) : make_int4(0, 0, 0, 0);
+            }
+        }
+        issue(c + kAttnRing - 1);
 #pragma unroll
         for (int u = 0; u < kAttnU; ++u) {
             const int j = j0 + u * kAttnKeysPerPass + slot;
@@ -717,25 +764,30 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cc_kernel(AttnArgs a) {
     }
 }
 
-template <int QB>
+template <int QB, bool RING>
 static cudaError_t attention_cc_launch(const AttnArgs &a, int B, int H, cudaStream_t st) {
     const int tk_cap = a.Tk_cap > 0 ? a.Tk_cap : a.Tk;
-    const size_t smem = (size_t)QB * tk_cap * 3;
+    const size_t smem = (RING ? (size_t)kAttnRing * kAttnU * kAttnKeysPerPass * 64 : 0) + (size_t)QB * tk_cap * 3;
     static size_t smem_set = 0;
     if (smem > 48 * 1024 && smem > smem_set) {
-        cudaError_t e = cudaFuncSetAttribute(attn_cc_kernel<QB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e =
+            cudaFuncSetAttribute(attn_cc_kernel<QB, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         smem_set = smem;
     }
     dim3 grid((a.Tq + QB - 1) / QB, H, B);
-    return launch_pdl(attn_cc_kernel<QB>, grid, kAttnThreads, smem, st, a);
+    return launch_pdl(attn_cc_kernel<QB, RING>, grid, kAttnThreads, smem, st, a);
 }
 
 cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
     if (B <= 0 || H <= 0 || a.Tq <= 0) return cudaSuccess;
     // one query row per CTA for decode steps; four otherwise (each CTA
     // re-reads K and V of its head, so wider query blocks save traffic)
-    return a.Tq <= 2 ? attention_cc_launch<1>(a, B, H, st) : attention_cc_launch<4>(a, B, H, st);
+    // (the K ring pays from ~1000 keys: measured on decode cross-attention
+    // over 1500 encoder states, neutral-to-negative on short self-attention)
+    const bool ring = (a.Tk_cap > 0 ? a.Tk_cap : a.Tk) >= 1024;
+    if (a.Tq <= 2) return ring ? attention_cc_launch<1, true>(a, B, H, st) : attention_cc_launch<1, false>(a, B, H, st);
+    return ring ? attention_cc_launch<4, true>(a, B, H, st) : attention_cc_launch<4, false>(a, B, H, st);
 }
 
 // ---------------------------------------------------------------------------
