@@ -54,8 +54,7 @@ constexpr int OFF_Q = 0;                          // two Q buffers
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
-constexpr int OFF_TAB = OFF_P + 2 * P_BYTES;
-constexpr int OFF_RED = OFF_TAB + TAB_MAX;        // [4][BQ] int32 cross-warp row reductions
+constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // [4][BQ] int32 cross-warp row reductions
 constexpr int OFF_BAR = OFF_RED + 4 * BQ * 4;
 constexpr int SMEM = 1024 + OFF_BAR + 512;
 constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
@@ -99,6 +98,15 @@ IW_DEV int32_t score_fast(uint32_t acc, uint32_t m, uint32_t rnd, uint32_t sh) {
     return y >> sh;
 }
 
+// (C - acc*m + [acc < 0]) mod 2^32 for negm = -m: two multiply-adds, the
+// second adding the sign bit of acc as the high word of acc * 2.
+IW_DEV uint32_t exp_index(uint32_t acc, uint32_t negm, uint32_t c) {
+    uint32_t t, u;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(t) : "r"(acc), "r"(negm), "r"(c));
+    asm("mad.hi.u32 %0, %1, 2, %2;" : "=r"(u) : "r"(acc), "r"(t));
+    return u;
+}
+
 IW_DEV int32_t rrs_masked(int32_t x, const AttnTcParams &p) {
     const uint32_t t = (uint32_t)x + p.qk_rnd + ((uint32_t)(x >> 31) & p.qk_sgn);
     return (int32_t)(((int32_t)t >> p.qk_sh) & (int32_t)p.qk_z);
@@ -115,7 +123,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     uint8_t *sK = smem + OFF_K;
     uint8_t *sV = smem + OFF_V;
     uint8_t *sP = smem + OFF_P;
-    uint8_t *sTab = smem + OFF_TAB;
+    // the shift-exp table lives in static shared memory: its address is a
+    // compile-time constant, so a lookup is one load with an immediate offset
+    __shared__ uint8_t sTab[TAB_MAX];
     int32_t *sRed = reinterpret_cast<int32_t *>(smem + OFF_RED);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *q_full = bars;                 // [2]
@@ -325,15 +335,27 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             mx = max(max(sRed[r], sRed[BQ + r]), max(sRed[2 * BQ + r], sRed[3 * BQ + r]));
             bar_soft();
             // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
-            int32_t smax = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
-            smax = clampi(smax, -32768, 32767);
+            const int32_t sraw = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
+            const int32_t smax = clampi(sraw, -32768, 32767);
             const int32_t rmax1 = (int32_t)(int16_t)(smax + 1);
             // For a row whose requantised max is below 32767 (no int16 wrap of
             // rowmax+1) and whose rowmax1 + 32768 >= t1, neither the int16 clamp
             // of a score nor the int16 wrap of its difference can change the
             // table index: idx = min(rowmax1 - s, t1) with s unclamped. The warp
             // uses that path only when all of its 32 rows qualify.
-            const bool warp_simple = __all_sync(0xffffffffu, rmax1 != -32768 && rmax1 + 32768 >= (int32_t)t1);
+            // On that path the index is computed from the raw score in two
+            // multiply-adds: with y = acc*m + rnd - [acc < 0] (the rounding
+            // shift's numerator, |acc*m| < 2^28) and the row's unclamped
+            // requantised max rowmax1 - 1 = y_max >> sh,
+            //   rowmax1 - (y >> sh) = (C - acc*m + [acc < 0]) >> sh,
+            //   C = (rowmax1 + 1) * 2^sh - 1 - rnd,
+            // where the numerator lies in [2^sh, 2^29 + 2^(sh+1)) and so is
+            // exact in unsigned 32-bit arithmetic for sh <= 30.
+            const bool warp_simple =
+                __all_sync(0xffffffffu, sraw > -32768 && sraw < 32767 && rmax1 + 32768 >= (int32_t)t1) &&
+                p.qk_sh <= 30;
+            const uint32_t cidx = ((uint32_t)(rmax1 + 1) << p.qk_sh) - 1u - p.qk_rnd;
+            const uint32_t negm = 0u - p.qk_mult;
             // ---- pass 2: exp, row sum, P to shared memory ----------------------
             int32_t rsum = 0;
             for (int j = 0; j < nkb; ++j) {
@@ -353,9 +375,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         uint32_t ww = 0;
 #pragma unroll
                         for (int k4 = 0; k4 < 4; ++k4) {
-                            const int32_t sc = score_fast(acc[q4 * 4 + k4], p.qk_mult, p.qk_rnd, p.qk_sh);
-                            const uint32_t idx = min((uint32_t)(rmax1 - sc), t1);
-                            ww += (uint32_t)sTab[idx] << (8 * k4);
+                            const uint32_t idx = min(exp_index(acc[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
+                            // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
+                            asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
                         }
                         rsum = __dp4a((int32_t)ww, 0x01010101, rsum);
                         w4[q4] = ww;
