@@ -59,6 +59,7 @@ SIGNATURES = {
     "iw_add_i32": [_P, _I32, _P],
     "iw_log_mel_int8": [_P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P],
     "iw_gelu_table": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P],
+    "iw_gelu_table_tiled": [_P, _I64, _P, _P],
     "iw_shift_exp_table": [_I32, _P, _P],
     "iw_linear8_noalloc": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
 }
@@ -82,7 +83,7 @@ class GemmDesc(C.Structure):
         ("out_rowsum", _P), ("tile_n", C.c_int), ("gelu_table", _P),
         ("vt_out", _P), ("vt_ld", _I64), ("vt_col0", _I64), ("vt_T", _I64),
         ("kv_cache_k", _P), ("kv_cache_v", _P), ("kv_col0", _I64), ("kv_heads", _I64), ("kv_T", _I64),
-        ("kv_Tcap", _I64), ("kv_pos", _I64), ("kv_pos_dev", _P),
+        ("kv_Tcap", _I64), ("kv_pos", _I64), ("kv_pos_dev", _P), ("gelu_table_tiled", _P),
     ]
 
 

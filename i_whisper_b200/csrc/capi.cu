@@ -421,6 +421,11 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     p.hm_B = (int)d->headmajor_B;
     p.rowsum_out = d->out_rowsum;
     p.gelu_tab = d->gelu_table;
+    if (d->gelu_table_tiled) {
+        if (!d->gelu_table || (reinterpret_cast<uintptr_t>(d->gelu_table_tiled) & 15))
+            return fail(IW_EINVAL, "iw_gemm_i8: gelu_table_tiled needs gelu_table and 16-byte alignment");
+        p.gelu_tab_tiled = d->gelu_table_tiled;
+    }
     if (d->kv_cache_k) {
         if (!d->kv_cache_v || d->mode != IW_GEMM_INT8 || d->vt_out || d->headmajor_T || d->transpose_T || d->pos ||
             d->kv_heads <= 0 || d->kv_T <= 0 || d->M % d->kv_T || d->kv_col0 < 0 || d->kv_col0 % 64 ||
@@ -468,6 +473,13 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
         return fail(IW_EINVAL, "iw_gemm_i8: gelu_table needs a per-channel int8 epilogue without lut");
     iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
     return cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8");
+}
+
+int iw_gelu_table_tiled(const int8_t *table, int64_t N, int8_t *tiled, void *stream) {
+    if (N <= 0 || N > (int64_t)1 << 30) return fail(IW_EINVAL, "iw_gelu_table_tiled: invalid N");
+    if (!table || !tiled || (reinterpret_cast<uintptr_t>(table) & 3) || (reinterpret_cast<uintptr_t>(tiled) & 15))
+        return fail(IW_EINVAL, "iw_gelu_table_tiled: table must be 4-byte and tiled 16-byte aligned");
+    return cuda_check(iw::gelu_table_tile(table, (int)N, tiled, S(stream)), "iw_gelu_table_tiled");
 }
 
 int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,

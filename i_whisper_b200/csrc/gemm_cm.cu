@@ -13,7 +13,9 @@
 //
 // Work split per CTA (one CTA per SM, persistent over tiles):
 //   warp 0      : TMA producer: per 128-deep k-block a 128x128 W tile and a
-//                 BRx128 X tile (128-byte swizzle, K-major) into a ring.
+//                 BRx128 X tile (128-byte swizzle, K-major) into a ring;
+//                 per tile, by bulk copies into a second pair of buffers,
+//                 the tile's input row sums and (pre-arranged) GeLU table.
 //   warp 1      : TMEM allocation (2*BR columns) and the single-thread
 //                 tcgen05.mma 128xBRx32 issue loop, committing stages and
 //                 accumulator buffers.
@@ -35,10 +37,10 @@ struct CmCfg {
     static constexpr int A_BYTES = 128 * kBlockK;  // W tile
     static constexpr int B_BYTES = BR * kBlockK;   // X tile
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int RS_BYTES = BR * 4;        // row sums of the tile's rows
+    static constexpr int RS_BYTES = BR * 4;        // row sums of the tile's rows (two buffers)
     static constexpr int PART_BYTES = 4 * BR * 4;  // per-quadrant partial output row sums
-    static constexpr int GTAB_BYTES = GK == 2 ? 128 * 256 : 0;  // the tile's GeLU table, lane-interleaved
-    static constexpr int FIXED = 1024 + 256 + RS_BYTES + PART_BYTES + GTAB_BYTES;
+    static constexpr int GTAB_BYTES = GK == 2 ? 128 * 256 : 0;  // the tile's GeLU table, lane-interleaved (two)
+    static constexpr int FIXED = 1024 + 256 + 2 * RS_BYTES + PART_BYTES + 2 * GTAB_BYTES;
     static constexpr int STAGES_FIT = (232448 - FIXED) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BR;
@@ -141,13 +143,15 @@ __global__ void __launch_bounds__(kCmThreads, 1)
     uint64_t *empty = full + S;
     uint64_t *tfull = empty + S;
     uint64_t *tempty = tfull + 2;
-    uint64_t *drain = tempty + 2;
+    uint64_t *aux_full = tempty + 2;   // [2] row sums / GeLU table of a tile landed
+    uint64_t *aux_empty = aux_full + 2;  // [2] the epilogue is done with them
+    uint64_t *drain = aux_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile uint32_t *abort_flag = tmem_slot + 1;
     volatile uint32_t *stop_s = tmem_slot + 2;
-    int32_t *rs_s = reinterpret_cast<int32_t *>(smem + S * Cfg::STAGE_BYTES + 256);
-    int32_t *part = rs_s + BR;
-    uint32_t *gtab_s = reinterpret_cast<uint32_t *>(part + 4 * BR);
+    int32_t *rs_s = reinterpret_cast<int32_t *>(smem + S * Cfg::STAGE_BYTES + 256);  // [2][BR]
+    int32_t *part = rs_s + 2 * BR;
+    uint32_t *gtab_s = reinterpret_cast<uint32_t *>(part + 4 * BR);  // [2][8192]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -155,6 +159,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
     const int row_tiles = (M + BR - 1) / BR;
     const int tiles = ch_tiles * row_tiles;
     const int kblocks = (K + kBlockK - 1) / kBlockK;
+    // Row sums of a full row tile come by one bulk copy when 16-byte aligned;
+    // the GeLU table does when given in the pre-arranged layout.
+    const bool rs_bulk = p.wz && (reinterpret_cast<uintptr_t>(p.rowsum) & 15) == 0;
+    const bool gt_bulk = GT && p.gelu_tab_tiled && (reinterpret_cast<uintptr_t>(p.gelu_tab_tiled) & 15) == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -164,6 +172,8 @@ __global__ void __launch_bounds__(kCmThreads, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], kCmEpiWarps);
+            mbar_init(&aux_full[b], 1);
+            mbar_init(&aux_empty[b], kCmEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -190,9 +200,25 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued_mask = 0, last_parity = 0;
+            int ab = 0;
+            uint32_t aph = 0, aux_issued = 0, aux_parity = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
                 const int m0 = (tile / ch_tiles) * BR;
                 const int n0 = (tile % ch_tiles) * 128;
+                {
+                    // the tile's epilogue inputs (an empty transaction when
+                    // the epilogue warps load them themselves)
+                    if (!mbar_wait(&aux_empty[ab], aph ^ 1)) { *abort_flag = 1; break; }
+                    const bool rs_t = rs_bulk && m0 + BR <= M;
+                    mbar_arrive_expect_tx(&aux_full[ab], (rs_t ? Cfg::RS_BYTES : 0) + (gt_bulk ? Cfg::GTAB_BYTES : 0));
+                    if (rs_t) bulk_load(rs_s + ab * BR, p.rowsum + m0, Cfg::RS_BYTES, &aux_full[ab]);
+                    if (gt_bulk)
+                        bulk_load(gtab_s + ab * 8192, p.gelu_tab_tiled + (int64_t)(n0 >> 7) * Cfg::GTAB_BYTES,
+                                  Cfg::GTAB_BYTES, &aux_full[ab]);
+                    aux_issued |= 1u << ab;
+                    aux_parity = (aux_parity & ~(1u << ab)) | (aph << ab);
+                    if (++ab == 2) { ab = 0; aph ^= 1; }
+                }
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
@@ -206,6 +232,8 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             // every copy this thread issued must land before the CTA exits
             for (int s = 0; s < S; ++s)
                 if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u);
+            for (int b = 0; b < 2; ++b)
+                if (aux_issued & (1u << b)) mbar_wait(&aux_full[b], (aux_parity >> b) & 1u);
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -253,24 +281,29 @@ __global__ void __launch_bounds__(kCmThreads, 1)
         }
         int buf = 0;
         uint32_t bphase = 0;
+        int ab = 0;
+        uint32_t aph = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int m0 = (tile / ch_tiles) * BR;
             const int n0 = (tile % ch_tiles) * 128;
+            int32_t *rs_t = rs_s + ab * BR;
+            uint32_t *gt_t = gtab_s + ab * 8192;
             // Barrier A: every epilogue warp is done with the previous tile's
-            // shared row sums and partials. One thread samples the abort flag
-            // so that all epilogue warps take the same decision.
+            // partial row sums. One thread samples the abort flag so that all
+            // epilogue warps take the same decision.
             cm_bar();
             if (et == 0) *stop_s = *abort_flag;
-            for (int i = et; i < BR; i += kCmEpiWarps * 32)
-                rs_s[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
-            if constexpr (GT) {
+            if (!(rs_bulk && m0 + BR <= M))
+                for (int i = et; i < BR; i += kCmEpiWarps * 32)
+                    rs_t[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
+            if (GT && !gt_bulk) {
                 // 16 table bytes of one channel per thread; a warp covers 32
                 // consecutive channels, so the four word stores hit 32 banks
                 for (int i = et; i < 128 * 16; i += kCmEpiWarps * 32) {
                     const int ch = i & 127, tq = i >> 7;
                     int4 t4 = make_int4(0, 0, 0, 0);
                     if (n0 + ch < N) t4 = __ldg(reinterpret_cast<const int4 *>(p.gelu_tab + (int64_t)(n0 + ch) * 256) + tq);
-                    uint32_t *dst = gtab_s + (ch >> 5) * 2048 + tq * 4 * 32 + (ch & 31);
+                    uint32_t *dst = gt_t + (ch >> 5) * 2048 + tq * 4 * 32 + (ch & 31);
                     dst[0] = (uint32_t)t4.x;
                     dst[32] = (uint32_t)t4.y;
                     dst[64] = (uint32_t)t4.z;
@@ -296,9 +329,11 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             // no correction and the rounding shift is three instructions.
             const bool simple = MODE == EPI_L8 && __all_sync(0xffffffffu, !cv || (ck.hmask == 0 && ck.q.sgn == -1));
 
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&tfull[buf], bphase);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            // every lane waits for the bulk copies (acquiring their data), lane 0
+            // for the accumulator
+            bool ok = mbar_wait(&aux_full[ab], aph);
+            if (lane == 0) ok = ok && mbar_wait(&tfull[buf], bphase);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0) *abort_flag = 1;
             } else {
@@ -311,7 +346,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                     tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BR + c * kCmCh),
                                        acc);
                     tmem_ld_wait();
-                    const int4 *rs4 = reinterpret_cast<const int4 *>(rs_s + c * kCmCh);
+                    const int4 *rs4 = reinterpret_cast<const int4 *>(rs_t + c * kCmCh);
                     int32_t v[kCmCh];
                     if (simple) {
 #pragma unroll
@@ -368,7 +403,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                         }
                     } else {
                         if constexpr (GT) {
-                            const uint32_t *gw = gtab_s + quad * 2048 + 32 * 32 + lane;
+                            const uint32_t *gw = gt_t + quad * 2048 + 32 * 32 + lane;
 #pragma unroll
                             for (int j = 0; j < kCmCh; ++j) v[j] = gelu_tab_k(v[j], gw);
                         } else if constexpr (GK == 1) {
@@ -477,10 +512,17 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                 }
             }
             tc_fence_before();
+            // this warp's shared-memory accesses to the tile's row sums and
+            // table come before the next bulk copy into the buffer
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (lane == 0) {
+                mbar_arrive(&tempty[buf]);
+                mbar_arrive(&aux_empty[ab]);
+            }
             buf ^= 1;
             if (buf == 0) bphase ^= 1;
+            if (++ab == 2) { ab = 0; aph ^= 1; }
             if (MODE == EPI_L8 && p.rowsum_out) {
                 // Barrier C: all four quadrants' partial sums of each row are in.
                 cm_bar();

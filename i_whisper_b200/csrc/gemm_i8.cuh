@@ -65,6 +65,10 @@ struct EpiParams {
     // indexed by (requantised value + 128); built by gelu_table_build from
     // the same GeLU parameters, so it is exact
     const int8_t *gelu_tab = nullptr;
+    // optional (channel-major path): the same table in the layout of
+    // gelu_table_tile (one 32 KB block per 128 channels, already in the
+    // kernel's shared-memory order), staged by one bulk copy per tile
+    const int8_t *gelu_tab_tiled = nullptr;
     // optional (channel-major path): int8 results of channels n >= tr_c0
     // are written per batch transposed, tr_out[(b*tr_N + n - tr_c0)*tr_ld + t]
     // with m = b*tr_T + t, instead of row-major (V^T for the attention)
@@ -83,6 +87,11 @@ struct EpiParams {
 // Builds tab[n][x+128] = GeLU_n(x) for x in [-128, 127] (gelu_scalar.cpp).
 cudaError_t gelu_table_build(const uint8_t *lut, const uint8_t *mi, const int8_t *si, const uint8_t *mo,
                              const int8_t *so, int n_in, int n_out, int N, int8_t *tab, cudaStream_t st);
+
+// Rearranges tab [N][256] into the channel-major GEMM's shared-memory order:
+// for each tile of 128 channels, 32-bit word q*2048 + r*32 + l holds bytes
+// 4r..4r+3 of channel 128*tile + 32q + l (zero past N).
+cudaError_t gelu_table_tile(const int8_t *tab, int N, int8_t *tiled, cudaStream_t st);
 
 struct GemmShape {
     const int8_t *x;

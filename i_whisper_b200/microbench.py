@@ -100,7 +100,10 @@ def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: 
                 tab = torch.empty(N, 256, dtype=torch.int8, device="cuda")
                 keep.append(tab)
                 _lib.call("iw_gelu_table", *[t.data_ptr() for t in gp], N, N, N, tab.data_ptr(), stream)
-                d.gelu_table = tab.data_ptr()
+                tiled = torch.empty((N + 127) // 128, 32768, dtype=torch.int8, device="cuda")
+                keep.append(tiled)
+                _lib.call("iw_gelu_table_tiled", tab.data_ptr(), N, tiled.data_ptr(), stream)
+                d.gelu_table, d.gelu_table_tiled = tab.data_ptr(), tiled.data_ptr()
             else:
                 d.lut, d.luti_multiplier, d.luti_shift, d.luto_multiplier, d.luto_shift = [t.data_ptr() for t in gp]
                 d.luti_per_channel = d.luto_per_channel = 1

@@ -257,6 +257,10 @@ typedef struct iw_gemm_desc {
     int8_t *kv_cache_v;
     int64_t kv_col0, kv_heads, kv_T, kv_Tcap, kv_pos;
     const int32_t *kv_pos_dev;
+    /* optional: gelu_table rearranged by iw_gelu_table_tiled (16-byte
+     * aligned); lets the kernel fetch each 128-channel tile's table with one
+     * bulk copy. gelu_table must still be given. */
+    const int8_t *gelu_table_tiled;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */
@@ -268,6 +272,12 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream);
 int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8_t *luti_shift,
                   const uint8_t *luto_multiplier, const int8_t *luto_shift, int64_t luti_count, int64_t luto_count,
                   int64_t N, int8_t *table, void *stream);
+
+/* Rearranges a [N][256] GeLU table (4-byte aligned) into tiled
+ * [ceil(N/128)][32768] bytes (16-byte aligned) for
+ * iw_gemm_desc.gelu_table_tiled: per 128 channels, 32-bit word
+ * q*2048 + r*32 + l holds bytes 4r..4r+3 of channel 32q + l (zero past N). */
+int iw_gelu_table_tiled(const int8_t *table, int64_t N, int8_t *tiled, void *stream);
 
 typedef struct iw_attn_desc {
     /* element (b,t,h,d) of Q is q[b*q_bs + t*ldq + h*q_hs + d], same for

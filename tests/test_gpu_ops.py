@@ -330,10 +330,13 @@ def test_device_status_clean():
     assert _lib.device_status(clear=True) == 0
 
 
-@pytest.mark.parametrize("M,K,N", [(300, 1024, 4096), (129, 384, 1536), (7, 1280, 5120)])
-def test_linear8_gelu_table_rowsum(ops, L, M, K, N):
+@pytest.mark.parametrize("tiled", [0, 1])
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 4096), (129, 384, 1536), (7, 1280, 5120), (515, 256, 1000),
+                                   (1024, 512, 2048)])
+def test_linear8_gelu_table_rowsum(ops, L, M, K, N, tiled):
     """fc1 form: Linear8 -> per-channel GeLU (lookup table) with the row sums
-    of the int8 output accumulated for the next GEMM's zero point."""
+    of the int8 output accumulated for the next GEMM's zero point; with
+    ``tiled`` the table also comes in the bulk-copy layout."""
     import ctypes
     from i_whisper_b200 import _lib
     rng = np.random.default_rng(M + N)
@@ -356,6 +359,18 @@ def test_linear8_gelu_table_rowsum(ops, L, M, K, N):
     d.mode, d.out, d.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
     d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
     d.gelu_table, d.out_rowsum = tab.data_ptr(), rs_out.data_ptr()
+    if tiled:
+        tt = torch.full(((N + 127) // 128, 32768), 77, dtype=torch.int8, device="cuda")
+        _lib.call("iw_gelu_table_tiled", tab.data_ptr(), N, tt.data_ptr(), st)
+        d.gelu_table_tiled = tt.data_ptr()
+        # the layout: word q*2048 + r*32 + l of tile t = bytes 4r..4r+3 of channel 128t + 32q + l
+        th, tb = host(tt).reshape(-1, 4, 64, 32, 4), host(tab)
+        n = np.arange(N)
+        got = th[n // 128, (n % 128) // 32, :, n % 32, :].reshape(N, 256)
+        assert np.array_equal(got, tb)
+        if N % 128:
+            pad = th.reshape(-1, 4, 64, 32, 4).transpose(0, 1, 3, 2, 4).reshape(-1, 128, 256)[-1, N % 128:]
+            assert not pad.any()
     _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
     assert np.array_equal(host(out), ref)
     assert np.array_equal(host(rs_out), ref.astype(np.int32).sum(1))
