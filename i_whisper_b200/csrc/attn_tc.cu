@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
     using namespace attn;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sK = smem + OFF_K;
     uint8_t *sV = smem + OFF_V;

@@ -120,10 +120,11 @@ IW_DEV int32_t gelu_k(int32_t x, const ChanK &c, const uint32_t (&lut)[4]) {
 // word q*2048 + (t/4)*32 + l, so the 32 lanes of a warp, whatever values
 // they look up, read 32 different banks. gw points at word q*2048 + 32*32 + l
 // (the +32 rows absorb the +128 offset of the value).
+// The result is the table byte zero-extended (the int8 bit pattern in bits
+// 0..7): every consumer of this path stores bytes or uses (v ^ 0x80) & 0xFF.
 IW_DEV int32_t gelu_tab_k(int32_t x, const uint32_t *gw) {
     const uint32_t w = gw[(x >> 2) * 32];
-    const uint32_t b = (uint32_t)x & 3u;
-    return (int32_t)(int8_t)(uint8_t)(w >> (b << 3));  // byte b, sign-extended
+    return (int32_t)__byte_perm(w, 0u, ((uint32_t)x & 3u) | 0x4440u);  // byte x&3, upper bytes 0
 }
 
 // GK: GeLU flavour of a Linear8 epilogue: 0 none, 1 from its parameters
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
     constexpr int S = Cfg::STAGES;
     constexpr bool GT = GK == 2;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;
     uint8_t *sB = smem + S * Cfg::A_BYTES;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
@@ -357,8 +358,14 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             for (int u = 0; u < 4; ++u) {
                                 const int j = 4 * q + u;
                                 const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
-                                const int32_t h = __mulhi(a, ck.mul);
-                                v[j] = clampi(u_add(u_add(h, ck.q.rnd), h >> 31) >> ck.q.sh, -127, 127);
+                                // rrs(mulh(a, mul), sh) = (h + rnd - [h < 0]) >> sh with
+                                // h = hi(a * mul); for 0 <= mul < 2^31 h has the sign of
+                                // a, so both corrections are multiply-adds:
+                                // t = hi(a * mul) + rnd, then t += hi(a * 1) (-1 or 0)
+                                int32_t t;
+                                asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(t) : "r"(a), "r"(ck.mul), "r"(ck.q.rnd));
+                                asm("mad.hi.s32 %0, %1, 1, %0;" : "+r"(t) : "r"(a));
+                                v[j] = clampi(t >> ck.q.sh, -127, 127);
                             }
                         }
                     } else {
@@ -410,11 +417,11 @@ __global__ void __launch_bounds__(kCmThreads, 1)
 #pragma unroll
                             for (int j = 0; j < kCmCh; ++j) v[j] = gelu_k(v[j], ck, lut);
                         }
-                        if (!cv) {
-#pragma unroll
-                            for (int j = 0; j < kCmCh; ++j) v[j] = 0;
-                        }
-                        if (p.posadd) {
+                        // (lanes of channels past N hold v = 0: the tensor map
+                        // zero-fills their weight rows and load_chan zeroes
+                        // their constants, so acc, the requantised value and
+                        // its GeLU are all 0)
+                        if (!GT && p.posadd) {  // (never with a GeLU table: its bytes are zero-extended)
                             // add_requant15_scalar.cpp:29-80, int16 result
                             if (cv) {
                                 int16_t *out = reinterpret_cast<int16_t *>(p.out);
@@ -482,12 +489,11 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             }
                         } else if (cv) {
                             int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= M) {
+                            if (r0 + kCmCh <= M && p.ldo < (1 << 27)) {
+                                // 32-bit row offsets: one wide multiply-add per address
+                                const uint32_t ldo32 = (uint32_t)p.ldo;
 #pragma unroll
-                                for (int j = 0; j < kCmCh; ++j) {
-                                    *out = (int8_t)v[j];
-                                    out += p.ldo;
-                                }
+                                for (int j = 0; j < kCmCh; ++j) out[(uint32_t)j * ldo32] = (int8_t)v[j];
                             } else {
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
@@ -497,15 +503,30 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             }
                         }
                         if (p.rowsum_out) {
-                            // per row, the sum over this warp's 32 channels
-                            int32_t rsum[kCmCh];
+                            // Per row, the sum over this warp's 32 channels, two
+                            // rows per reduction: each lane adds v + 128 (0..255,
+                            // from the low byte whether v is sign- or
+                            // zero-extended) into one 16-bit half, so a half
+                            // totals at most 32 * 255 and the row sum is that
+                            // total - 32 * 128 (lanes of channels past N hold 0).
+                            uint32_t rsum[kCmCh / 2];
 #pragma unroll
-                            for (int j = 0; j < kCmCh; ++j) rsum[j] = __reduce_add_sync(0xffffffffu, v[j]);
+                            for (int j = 0; j < kCmCh / 2; ++j) {
+                                uint32_t w;  // v0 + v1 * 2^16
+                                asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(w) : "r"(v[2 * j + 1]), "r"(v[2 * j]));
+                                // zero-extended bytes (GeLU table): flip the sign bits;
+                                // sign-extended values: add 128 to each half
+                                w = GT ? (w ^ 0x00800080u) : (w + 0x00800080u);
+                                rsum[j] = __reduce_add_sync(0xffffffffu, w);
+                            }
                             if (lane == 0) {
                                 int4 *dst = reinterpret_cast<int4 *>(part + quad * BR + c * kCmCh);
 #pragma unroll
                                 for (int q4 = 0; q4 < kCmCh / 4; ++q4)
-                                    dst[q4] = make_int4(rsum[4 * q4], rsum[4 * q4 + 1], rsum[4 * q4 + 2], rsum[4 * q4 + 3]);
+                                    dst[q4] = make_int4((int32_t)(rsum[2 * q4] & 0xFFFFu) - 4096,
+                                                        (int32_t)(rsum[2 * q4] >> 16) - 4096,
+                                                        (int32_t)(rsum[2 * q4 + 1] & 0xFFFFu) - 4096,
+                                                        (int32_t)(rsum[2 * q4 + 1] >> 16) - 4096);
                             }
                         }
                     }

@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using Cfg = GemmCfg<BN, FLAVOR>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = smem_align1024(smem_raw);
     uint8_t *sA = smem;
     uint8_t *sB = smem + S * Cfg::A_BYTES;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);

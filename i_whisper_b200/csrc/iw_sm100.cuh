@@ -22,6 +22,12 @@ namespace iw {
 
 IW_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// The dynamic shared array rounded up to a 1024-byte boundary (swizzled
+// operand tiles). Offsetting the array itself, rather than rounding a
+// generic address, keeps the pointer in the shared address space, so every
+// access through it is a shared-memory instruction with a 32-bit address.
+IW_DEV uint8_t *smem_align1024(uint8_t *raw) { return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u); }
+
 IW_DEV uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -51,13 +57,27 @@ IW_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait that may suspend the thread for up to `hint_ns` (it resumes as
+// soon as the phase completes): a waiting warp then takes no issue slots
+// from the warps doing the work.
+IW_DEV bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase with the given parity. Returns false (and
 // records IW_DEVERR_WAIT_TIMEOUT) if it did not complete in time.
 IW_DEV bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, 200000u)) return true;
         if ((it & 255u) == 0 && globaltimer_ns() - t0 > IW_WAIT_TIMEOUT_NS) {
             atomicOr(&g_device_status, IW_DEVERR_WAIT_TIMEOUT);
             return false;
