@@ -115,17 +115,14 @@ IW_DEV int32_t gelu_k(int32_t x, const ChanK &c, const uint32_t (&lut)[4]) {
     return clampi(v, -127, 127);
 }
 
-// GeLU through the tile's table in shared memory. The table of channel
-// (quadrant q, lane l) holds its 256 results with byte t (value t - 128) in
-// word q*2048 + (t/4)*32 + l, so the 32 lanes of a warp, whatever values
-// they look up, read 32 different banks. gw points at word q*2048 + 32*32 + l
-// (the +32 rows absorb the +128 offset of the value).
-// The result is the table byte zero-extended (the int8 bit pattern in bits
-// 0..7): every consumer of this path stores bytes or uses (v ^ 0x80) & 0xFF.
-IW_DEV int32_t gelu_tab_k(int32_t x, const uint32_t *gw) {
-    const uint32_t w = gw[(x >> 2) * 32];
-    return (int32_t)__byte_perm(w, 0u, ((uint32_t)x & 3u) | 0x4440u);  // byte x&3, upper bytes 0
-}
+// GeLU through the tile's table in shared memory: the result for value x
+// of channel (quadrant q, lane l) is byte q*8192 + (x + 128)*32 + l, so a
+// lookup is one multiply-add and one byte load (the lanes of a 4-lane group
+// share a bank word per value; other lanes never conflict). gb points at
+// byte q*8192 + 128*32 + l. The result is the table byte zero-extended (the
+// int8 bit pattern in bits 0..7): every consumer of this path stores bytes
+// or uses (v ^ 0x80) & 0xFF.
+IW_DEV int32_t gelu_tab_k(int32_t x, const uint8_t *gb) { return (int32_t)gb[x * 32]; }
 
 // GK: GeLU flavour of a Linear8 epilogue: 0 none, 1 from its parameters
 // (ALU), 2 from the per-channel lookup table.
@@ -298,17 +295,17 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                 for (int i = et; i < BR; i += kCmEpiWarps * 32)
                     rs_t[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
             if (GT && !gt_bulk) {
-                // 16 table bytes of one channel per thread; a warp covers 32
-                // consecutive channels, so the four word stores hit 32 banks
+                // 16 table bytes of one channel per thread, scattered into
+                // the lookup layout (used only without the pre-arranged table)
+                uint8_t *gb = reinterpret_cast<uint8_t *>(gt_t);
                 for (int i = et; i < 128 * 16; i += kCmEpiWarps * 32) {
                     const int ch = i & 127, tq = i >> 7;
                     int4 t4 = make_int4(0, 0, 0, 0);
                     if (n0 + ch < N) t4 = __ldg(reinterpret_cast<const int4 *>(p.gelu_tab + (int64_t)(n0 + ch) * 256) + tq);
-                    uint32_t *dst = gt_t + (ch >> 5) * 2048 + tq * 4 * 32 + (ch & 31);
-                    dst[0] = (uint32_t)t4.x;
-                    dst[32] = (uint32_t)t4.y;
-                    dst[64] = (uint32_t)t4.z;
-                    dst[96] = (uint32_t)t4.w;
+                    const uint32_t w[4] = {(uint32_t)t4.x, (uint32_t)t4.y, (uint32_t)t4.z, (uint32_t)t4.w};
+                    uint8_t *dst = gb + (ch >> 5) * 8192 + tq * 16 * 32 + (ch & 31);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) dst[k * 32] = (uint8_t)(w[k >> 2] >> (8 * (k & 3)));
                 }
             }
             cm_bar();
@@ -410,9 +407,9 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                         }
                     } else {
                         if constexpr (GT) {
-                            const uint32_t *gw = gt_t + quad * 2048 + 32 * 32 + lane;
+                            const uint8_t *gb = reinterpret_cast<const uint8_t *>(gt_t) + quad * 8192 + 128 * 32 + lane;
 #pragma unroll
-                            for (int j = 0; j < kCmCh; ++j) v[j] = gelu_tab_k(v[j], gw);
+                            for (int j = 0; j < kCmCh; ++j) v[j] = gelu_tab_k(v[j], gb);
                         } else if constexpr (GK == 1) {
 #pragma unroll
                             for (int j = 0; j < kCmCh; ++j) v[j] = gelu_k(v[j], ck, lut);

@@ -658,20 +658,19 @@ cudaError_t gelu_table_build(const uint8_t *lut, const uint8_t *mi, const int8_t
     return cudaGetLastError();
 }
 
-__global__ void gelu_table_tile_kernel(const uint32_t *tab, int N, uint32_t *tiled, int64_t words) {
+__global__ void gelu_table_tile_kernel(const int8_t *tab, int N, int8_t *tiled, int64_t bytes) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= words) return;
-    const int64_t tile = i >> 13;
-    const int w = (int)(i & 8191), q = w >> 11, r = (w >> 5) & 63, l = w & 31;
+    if (i >= bytes) return;
+    const int64_t tile = i >> 15;
+    const int o = (int)(i & 32767), q = o >> 13, t = (o >> 5) & 255, l = o & 31;
     const int64_t n = tile * 128 + q * 32 + l;
-    tiled[i] = n < N ? tab[n * 64 + r] : 0u;
+    tiled[i] = n < N ? tab[n * 256 + t] : (int8_t)0;
 }
 
 cudaError_t gelu_table_tile(const int8_t *tab, int N, int8_t *tiled, cudaStream_t st) {
-    const int64_t words = (int64_t)((N + 127) / 128) * 8192;
-    if (words <= 0) return cudaSuccess;
-    gelu_table_tile_kernel<<<(unsigned)((words + 255) / 256), 256, 0, st>>>(
-        reinterpret_cast<const uint32_t *>(tab), N, reinterpret_cast<uint32_t *>(tiled), words);
+    const int64_t bytes = (int64_t)((N + 127) / 128) * 32768;
+    if (bytes <= 0) return cudaSuccess;
+    gelu_table_tile_kernel<<<(unsigned)((bytes + 255) / 256), 256, 0, st>>>(tab, N, tiled, bytes);
     return cudaGetLastError();
 }
 

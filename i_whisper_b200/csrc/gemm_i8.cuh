@@ -89,8 +89,8 @@ cudaError_t gelu_table_build(const uint8_t *lut, const uint8_t *mi, const int8_t
                              const int8_t *so, int n_in, int n_out, int N, int8_t *tab, cudaStream_t st);
 
 // Rearranges tab [N][256] into the channel-major GEMM's shared-memory order:
-// for each tile of 128 channels, 32-bit word q*2048 + r*32 + l holds bytes
-// 4r..4r+3 of channel 128*tile + 32q + l (zero past N).
+// for each tile of 128 channels, byte q*8192 + t*32 + l holds entry t of
+// channel 128*tile + 32q + l (zero past N).
 cudaError_t gelu_table_tile(const int8_t *tab, int N, int8_t *tiled, cudaStream_t st);
 
 struct GemmShape {

@@ -273,10 +273,9 @@ int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8
                   const uint8_t *luto_multiplier, const int8_t *luto_shift, int64_t luti_count, int64_t luto_count,
                   int64_t N, int8_t *table, void *stream);
 
-/* Rearranges a [N][256] GeLU table (4-byte aligned) into tiled
- * [ceil(N/128)][32768] bytes (16-byte aligned) for
- * iw_gemm_desc.gelu_table_tiled: per 128 channels, 32-bit word
- * q*2048 + r*32 + l holds bytes 4r..4r+3 of channel 32q + l (zero past N). */
+/* Rearranges a [N][256] GeLU table into tiled [ceil(N/128)][32768] bytes
+ * (16-byte aligned) for iw_gemm_desc.gelu_table_tiled: per 128 channels,
+ * byte q*8192 + t*32 + l holds entry t of channel 32q + l (zero past N). */
 int iw_gelu_table_tiled(const int8_t *table, int64_t N, int8_t *tiled, void *stream);
 
 typedef struct iw_attn_desc {

@@ -363,13 +363,13 @@ def test_linear8_gelu_table_rowsum(ops, L, M, K, N, tiled):
         tt = torch.full(((N + 127) // 128, 32768), 77, dtype=torch.int8, device="cuda")
         _lib.call("iw_gelu_table_tiled", tab.data_ptr(), N, tt.data_ptr(), st)
         d.gelu_table_tiled = tt.data_ptr()
-        # the layout: word q*2048 + r*32 + l of tile t = bytes 4r..4r+3 of channel 128t + 32q + l
-        th, tb = host(tt).reshape(-1, 4, 64, 32, 4), host(tab)
+        # the layout: byte q*8192 + e*32 + l of tile t = entry e of channel 128t + 32q + l
+        th, tb = host(tt).reshape(-1, 4, 256, 32), host(tab)
         n = np.arange(N)
-        got = th[n // 128, (n % 128) // 32, :, n % 32, :].reshape(N, 256)
+        got = th[n // 128, (n % 128) // 32, :, n % 32]
         assert np.array_equal(got, tb)
         if N % 128:
-            pad = th.reshape(-1, 4, 64, 32, 4).transpose(0, 1, 3, 2, 4).reshape(-1, 128, 256)[-1, N % 128:]
+            pad = th.transpose(0, 1, 3, 2).reshape(-1, 128, 256)[-1, N % 128:]
             assert not pad.any()
     _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
     assert np.array_equal(host(out), ref)
