@@ -325,7 +325,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             // Checkpoints made by the quantiser's frexp rule have multipliers
             // below 2^31 and shifts in [1, 31]; for such a warp the MULH needs
             // no correction and the rounding shift is three instructions.
-            const bool simple = MODE == EPI_L8 && __all_sync(0xffffffffu, !cv || (ck.hmask == 0 && ck.q.sgn == -1));
+            // Linear32: multipliers below 2^31 and shifts below 32 make it a
+            // plain high product and left shift.
+            const bool simple = __all_sync(
+                0xffffffffu, !cv || (ck.hmask == 0 && (MODE == EPI_L8 ? ck.q.sgn == -1 : ck.q.z == -1)));
 
             // every lane waits for the bulk copies (acquiring their data), lane 0
             // for the accumulator
@@ -355,6 +358,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             for (int u = 0; u < 4; ++u) {
                                 const int j = 4 * q + u;
                                 const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                if constexpr (MODE != EPI_L8) {
+                                    v[j] = (int32_t)((uint32_t)__mulhi(a, ck.mul) << ck.q.sh);
+                                    continue;
+                                }
                                 // rrs(mulh(a, mul), sh) = (h + rnd - [h < 0]) >> sh with
                                 // h = hi(a * mul); for 0 <= mul < 2^31 h has the sign of
                                 // a, so both corrections are multiply-adds:
@@ -392,16 +399,30 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             // load the chunk's 32 residuals before the first store so
                             // the loads overlap instead of waiting on each store.
                             int32_t rv[kCmCh];
+                            const int16_t *res = p.res + (int64_t)r0 * p.ldr + n;
+                            int16_t *o16 = out + (int64_t)r0 * p.ldo + n;
+                            if (r0 + kCmCh <= M && p.ldr < (1 << 26) && p.ldo < (1 << 26)) {
+                                // whole chunk: 32-bit row offsets
+                                const uint32_t ldr32 = (uint32_t)p.ldr, ldo32 = (uint32_t)p.ldo;
 #pragma unroll
-                            for (int j = 0; j < kCmCh; ++j)
-                                rv[j] = (r0 + j < M) ? (int32_t)p.res[(int64_t)(r0 + j) * p.ldr + n] : 0;
+                                for (int j = 0; j < kCmCh; ++j) rv[j] = res[(uint32_t)j * ldr32];
 #pragma unroll
-                            for (int j = 0; j < kCmCh; ++j) {
-                                const int64_t m = r0 + j;
-                                if (m < M) {
+                                for (int j = 0; j < kCmCh; ++j) {
                                     int32_t t = u_mad(rv[j], rm, v[j]);
                                     t = u_add(u_add(t, 1 << 14), t >> 31) >> 15;
-                                    out[m * p.ldo + n] = (int16_t)clampi(t, -16383, 16383);
+                                    o16[(uint32_t)j * ldo32] = (int16_t)clampi(t, -16383, 16383);
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < kCmCh; ++j)
+                                    rv[j] = (r0 + j < M) ? (int32_t)res[(int64_t)j * p.ldr] : 0;
+#pragma unroll
+                                for (int j = 0; j < kCmCh; ++j) {
+                                    if (r0 + j < M) {
+                                        int32_t t = u_mad(rv[j], rm, v[j]);
+                                        t = u_add(u_add(t, 1 << 14), t >> 31) >> 15;
+                                        o16[(int64_t)j * p.ldo] = (int16_t)clampi(t, -16383, 16383);
+                                    }
                                 }
                             }
                         }
@@ -586,14 +607,13 @@ static cudaError_t launch_cm_mode(const GemmShape &g, const EpiParams &p, cudaSt
 }
 
 // The channel-major path covers Linear8 (per-channel or scalar requant,
-// optional GeLU from its parameters, positional add, row-major, head-major
-// or per-batch transposed int8 output, optional output row sums) and
-// Linear32 + Residual15. GeLU lookup tables are a row-major-path feature.
+// optional GeLU from its parameters or a per-channel lookup table,
+// positional add, row-major, head-major, KV-cache or per-batch transposed
+// int8 output, optional output row sums) and Linear32 + Residual15.
 bool cm_eligible(const GemmShape &g, EpiMode mode, const EpiParams &p) {
-    // Linear32 + Residual15 stays on the row-major kernel, which reads and
-    // writes the INT15 residual rows with 16-byte accesses and measured
-    // faster (2141 vs 2083 TOPS at K=4096, 790 vs 600 at K=1024).
-    if (mode != EPI_L8) return false;
+    // Linear8 and Linear32 + Residual15 (measured 1030 vs 864 TOPS at
+    // K=1024 and 2241 vs 2157 at K=4096 against the row-major kernel).
+    if (mode != EPI_L8 && mode != EPI_L32_RES) return false;
     if (p.vt_T) return false;
     if (p.gelu_tab && (p.gelu || !p.per_channel || p.posadd)) return false;
     if (mode == EPI_L32_RES && (!p.per_channel || p.gelu || p.posadd || p.hm_T || p.tr_out || p.rowsum_out))
