@@ -284,13 +284,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const uint32_t col = (uint32_t)(slice * 32);
         int sb = 0, pb = 0, ob = 0;
         uint32_t sph = 0, pph = 0, oph = 0;
-        // wait helper: lane 0 waits, the warp agrees; once a wait failed the
-        // warp stops waiting (and computing) but keeps meeting the barriers
+        // wait helper: every lane waits (the warp stays converged, which
+        // measured faster than one lane waiting for the others), the warp
+        // agrees; once a wait failed the warp stops waiting (and computing)
+        // but keeps meeting the barriers
         bool ok = true;
         auto wait_all = [&](uint64_t *bar, uint32_t parity) {
             bool w = ok;
-            if (ok && lane == 0) w = mbar_wait(bar, parity);
-            w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+            if (ok) w = mbar_wait(bar, parity);
+            w = __all_sync(0xffffffffu, w);
             if (!w && ok) {
                 ok = false;
                 if (lane == 0) *abort_flag = 1;

@@ -330,10 +330,9 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             const bool simple = __all_sync(
                 0xffffffffu, !cv || (ck.hmask == 0 && (MODE == EPI_L8 ? ck.q.sgn == -1 : ck.q.z == -1)));
 
-            // every lane waits for the bulk copies (acquiring their data), lane 0
-            // for the accumulator
-            bool ok = mbar_wait(&aux_full[ab], aph);
-            if (lane == 0) ok = ok && mbar_wait(&tfull[buf], bphase);
+            // every lane waits (the warp stays converged) for the bulk copies,
+            // acquiring their data, and for the accumulator
+            bool ok = mbar_wait(&aux_full[ab], aph) && mbar_wait(&tfull[buf], bphase);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0) *abort_flag = 1;

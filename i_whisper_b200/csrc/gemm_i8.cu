@@ -467,9 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 epi_bar();
                 if (stop) break;
             }
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&tfull[buf], bphase);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            bool ok = mbar_wait(&tfull[buf], bphase);  // every lane: the warp stays converged
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0) *abort_flag = 1;
                 if constexpr (FLAVOR == 0) break;
