@@ -20,8 +20,9 @@
 // exactly; no rescaling of partial sums is needed.
 //
 // Warp roles: warp 0 TMA producer (Q once, K blocks twice, V^T blocks),
-// warp 1 TMEM owner + MMA issuer, warps 2..9 softmax (thread = query row of
-// its TMEM lane quadrant, two warps per quadrant split the 128 key columns).
+// warp 1 TMEM owner + P.V issuer, warp 18 Q.K^T issuer, warps 2..17 softmax
+// (thread = query row of its TMEM lane quadrant, four warps per quadrant
+// split the 128 key columns).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -41,8 +42,16 @@ constexpr int BK = 128;     // keys per block
 constexpr int KST = 4;      // K stages
 constexpr int VST = 3;      // V^T stages
 constexpr int SBUF = 3;     // S accumulators in TMEM
-constexpr int SOFT_WARPS = 16;  // four per TMEM lane quadrant, 32 keys each
-constexpr int THREADS = 64 + 32 * SOFT_WARPS;
+// Softmax warps: SLICES per TMEM lane quadrant, each taking SC of a block's
+// 128 keys (sixteen warps of 32 keys measured faster than eight of 64).
+constexpr int SOFT_WARPS = 16;
+constexpr int SLICES = SOFT_WARPS / 4;
+constexpr int SC = BK / SLICES;       // keys per warp and block
+constexpr int HALVES = SC / 32;       // 32-column TMEM loads per block
+constexpr int OC = 64 / SLICES;       // output columns per warp
+constexpr int QK_WARP = 2 + SOFT_WARPS;  // the Q.K^T issuer
+constexpr int THREADS = 96 + 32 * SOFT_WARPS;
+static_assert(SC % 32 == 0 && (OC == 16 || OC == 32), "softmax warp split");
 constexpr int TAB_MAX = 4096;  // entries of the shift-exp table kept in shared memory
 
 constexpr int Q_BYTES = BQ * 64;
@@ -54,7 +63,7 @@ constexpr int OFF_Q = 0;                          // two Q buffers
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
-constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // [4][BQ] int32 cross-warp row reductions
+constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // [SLICES][BQ] int32 cross-warp row reductions
 constexpr int OFF_BAR = OFF_RED + 4 * BQ * 4;
 constexpr int SMEM = 1024 + OFF_BAR + 512;
 constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
@@ -162,7 +171,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int s = 0; s < KST; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
         for (int s = 0; s < VST; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
         for (int s = 0; s < SBUF; ++s) { mbar_init(&s_full[s], 1); mbar_init(&s_empty[s], SOFT_WARPS); }
-        mbar_init(drain, 1);
+        mbar_init(drain, 2);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -209,68 +218,79 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             }
             if (!ok) *abort_flag = 1;
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == QK_WARP) {
+        // Two MMA issuers on different sub-partitions: QK_WARP issues every
+        // Q.K^T (bounded by the free S buffers, so it runs ahead of the
+        // softmax), warp 1 every P.V (after the softmax has written P).
         if (lane == 0) {
-            constexpr uint32_t idesc_qk = idesc_i8(BQ, BK, true, true);
-            constexpr uint32_t idesc_pv = idesc_i8(BQ, 64, false, true);
-            int qs = 0, ks = 0, sb = 0, pb = 0, vs = 0, ob = 0;
-            uint32_t qph = 0, kph = 0, sph = 0, pph = 0, vph = 0, oph = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
-                if (!mbar_wait(&q_full[qs], qph)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t qa = smem_u32(sQ + qs * Q_BYTES);
-                auto issue_qk = [&]() -> bool {
-                    if (!mbar_wait(&s_empty[sb], sph ^ 1)) return false;
-                    if (!mbar_wait(&k_full[ks], kph)) return false;
+            if (warp == QK_WARP) {
+                constexpr uint32_t idesc_qk = idesc_i8(BQ, BK, true, true);
+                int qs = 0, ks = 0, sb = 0;
+                uint32_t qph = 0, kph = 0, sph = 0;
+                for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
+                    if (!mbar_wait(&q_full[qs], qph)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t ka = smem_u32(sK + ks * K_BYTES);
-                    const uint32_t d = tmem_base + (uint32_t)(sb * BK);
+                    const uint32_t qa = smem_u32(sQ + qs * Q_BYTES);
+                    for (int pass = 0; pass < 2 && ok; ++pass) {
+                        for (int j = 0; j < nkb; ++j) {
+                            if (!mbar_wait(&s_empty[sb], sph ^ 1) || !mbar_wait(&k_full[ks], kph)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t ka = smem_u32(sK + ks * K_BYTES);
+                            const uint32_t d = tmem_base + (uint32_t)(sb * BK);
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk)
-                        mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
-                    mma_commit(&k_empty[ks]);
-                    mma_commit(&s_full[sb]);
-                    if (++ks == KST) { ks = 0; kph ^= 1; }
-                    if (++sb == SBUF) { sb = 0; sph ^= 1; }
-                    return true;
-                };
-                // pass 1
-                for (int j = 0; j < nkb && ok; ++j) ok = issue_qk();
-                // pass 2: QK of block j+1 is issued before P.V of block j
-                if (ok) ok = issue_qk();
-                for (int j = 0; j < nkb && ok; ++j) {
-                    if (j + 1 < nkb) ok = issue_qk();
+                            for (int kk = 0; kk < 2; ++kk)
+                                mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
+                            mma_commit(&k_empty[ks]);
+                            mma_commit(&s_full[sb]);
+                            if (++ks == KST) { ks = 0; kph ^= 1; }
+                            if (++sb == SBUF) { sb = 0; sph ^= 1; }
+                        }
+                    }
                     if (!ok) break;
-                    if (j + 1 == nkb) mma_commit(&q_empty[qs]);  // every QK of this item issued
-                    if (!mbar_wait(&p_full[pb], pph) || !mbar_wait(&v_full[vs], vph)) { ok = false; break; }
-                    if (j == 0 && !mbar_wait(&o_empty[ob], oph ^ 1)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t pa = smem_u32(sP + pb * P_BYTES);
-                    const uint32_t va = smem_u32(sV + vs * V_BYTES);
-                    const uint32_t tO = tmem_base + TMEM_O + (uint32_t)(ob * 64);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 32; ++kk)
-                        mma_i8(tO, sdesc_kmajor_sw128(pa + kk * 32), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
-                               (j | kk) != 0);
-                    mma_commit(&v_empty[vs]);
-                    mma_commit(&p_empty[pb]);
-                    if (++vs == VST) { vs = 0; vph ^= 1; }
-                    if (++pb == 2) { pb = 0; pph ^= 1; }
+                    mma_commit(&q_empty[qs]);  // every QK of this item issued
+                    if (++qs == 2) { qs = 0; qph ^= 1; }
                 }
-                if (!ok) break;
-                mma_commit(&o_full[ob]);
-                if (++ob == 2) { ob = 0; oph ^= 1; }
-                if (++qs == 2) { qs = 0; qph ^= 1; }
+            } else {
+                constexpr uint32_t idesc_pv = idesc_i8(BQ, 64, false, true);
+                int pb = 0, vs = 0, ob = 0;
+                uint32_t pph = 0, vph = 0, oph = 0;
+                for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
+                    for (int j = 0; j < nkb; ++j) {
+                        if (!mbar_wait(&p_full[pb], pph) || !mbar_wait(&v_full[vs], vph)) { ok = false; break; }
+                        if (j == 0 && !mbar_wait(&o_empty[ob], oph ^ 1)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t pa = smem_u32(sP + pb * P_BYTES);
+                        const uint32_t va = smem_u32(sV + vs * V_BYTES);
+                        const uint32_t tO = tmem_base + TMEM_O + (uint32_t)(ob * 64);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; ++kk)
+                            mma_i8(tO, sdesc_kmajor_sw128(pa + kk * 32), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
+                                   (j | kk) != 0);
+                        mma_commit(&v_empty[vs]);
+                        mma_commit(&p_empty[pb]);
+                        if (++vs == VST) { vs = 0; vph ^= 1; }
+                        if (++pb == 2) { pb = 0; pph ^= 1; }
+                    }
+                    if (!ok) break;
+                    mma_commit(&o_full[ob]);
+                    if (++ob == 2) { ob = 0; oph ^= 1; }
+                }
             }
             if (!ok) *abort_flag = 1;
+            // every MMA this thread issued completes before TMEM is released
+            // (the barrier counts both issuers' commits)
             mma_commit(drain);
             mbar_wait(drain, 0);
         }
     } else {
         // ------------------------------------------------------------------
         // softmax warps: thread = query row of the warp's TMEM lane quadrant,
-        // the warp's slice = 32 of the 128 key columns of every block
+        // the warp's slice = SC of the 128 key columns of every block, taken
+        // as HALVES 32-column halves
         // ------------------------------------------------------------------
         const int sw = warp - 2;
         const int quad = warp & 3;
@@ -281,7 +301,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const uint32_t t1 = min((uint32_t)p.tab[0] | ((uint32_t)p.tab[1] << 8), (uint32_t)(TAB_MAX - 1));
         for (uint32_t i = et; i <= t1; i += SOFT_WARPS * 32) sTab[i] = p.tab[2 + i];
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        const uint32_t col = (uint32_t)(slice * 32);
+        const uint32_t col = (uint32_t)(slice * SC);
         int sb = 0, pb = 0, ob = 0;
         uint32_t sph = 0, pph = 0, oph = 0;
         // wait helper: every lane waits (the warp stays converged, which
@@ -299,6 +319,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             }
             return ok;
         };
+        auto ld_half = [&](int sbuf, int hf, uint32_t (&a)[32]) {
+            tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sbuf * BK) + col + (uint32_t)(hf * 32), a);
+        };
         for (int it = blockIdx.x; it < items; it += gridDim.x) {
             // every softmax warp reads the abort flag between the same two
             // barriers (it is only written outside them) and leaves together
@@ -314,27 +337,32 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             for (int j = 0; j < nkb; ++j) {
                 if (!wait_all(&s_full[sb], sph)) break;
                 tc_fence_after();
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK) + col, acc);
+                uint32_t acc[HALVES][32];
+#pragma unroll
+                for (int hf = 0; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
                 tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_empty[sb]);  // S is in registers: release it early
-                const int valid = T - (j * BK + slice * 32);
-                if (valid >= 32) {
 #pragma unroll
-                    for (int u = 0; u < 32; ++u) mx = max(mx, (int32_t)acc[u]);
-                } else {
+                for (int hf = 0; hf < HALVES; ++hf) {
+                    const int valid = T - (j * BK + slice * SC + hf * 32);
+                    if (valid >= 32) {
 #pragma unroll
-                    for (int u = 0; u < 32; ++u)
-                        if (u < valid) mx = max(mx, (int32_t)acc[u]);
+                        for (int u = 0; u < 32; ++u) mx = max(mx, (int32_t)acc[hf][u]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 32; ++u)
+                            if (u < valid) mx = max(mx, (int32_t)acc[hf][u]);
+                    }
                 }
                 if (++sb == SBUF) { sb = 0; sph ^= 1; }
             }
-            // combine the four column slices of each row
+            // combine the column slices of each row
             sRed[slice * BQ + r] = mx;
             bar_soft();
-            mx = max(max(sRed[r], sRed[BQ + r]), max(sRed[2 * BQ + r], sRed[3 * BQ + r]));
+#pragma unroll
+            for (int sl = 0; sl < SLICES; ++sl) mx = max(mx, sRed[sl * BQ + r]);
             bar_soft();
             // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
             const int32_t sraw = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
@@ -358,55 +386,69 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                 p.qk_sh <= 30;
             const uint32_t cidx = ((uint32_t)(rmax1 + 1) << p.qk_sh) - 1u - p.qk_rnd;
             const uint32_t negm = 0u - p.qk_mult;
-            // ---- pass 2: exp, row sum, P to shared memory ----------------------
-            int32_t rsum = 0;
-            for (int j = 0; j < nkb; ++j) {
-                if (!wait_all(&s_full[sb], sph)) break;
-                tc_fence_after();
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sb * BK) + col, acc);
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[sb]);
-                const int valid = T - (j * BK + slice * 32);
-                uint32_t w4[8];
+            // exp of 32 scores of one half into eight packed words, adding to rsum
+            auto exp_half = [&](const uint32_t (&a)[32], int valid, uint32_t (&w4)[8], int32_t &rs) {
                 if (FAST && warp_simple && valid >= 32) {
 #pragma unroll
                     for (int q4 = 0; q4 < 8; ++q4) {
                         uint32_t ww = 0;
 #pragma unroll
                         for (int k4 = 0; k4 < 4; ++k4) {
-                            const uint32_t idx = min(exp_index(acc[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
+                            const uint32_t idx = min(exp_index(a[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
                             // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
                             asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
                         }
-                        rsum = __dp4a((int32_t)ww, 0x01010101, rsum);
+                        rs = __dp4a((int32_t)ww, 0x01010101, rs);
                         w4[q4] = ww;
                     }
                 } else {
 #pragma unroll
                     for (int u = 0; u < 32; ++u) {
                         int32_t sc;
-                        if constexpr (FAST) sc = score_fast(acc[u], p.qk_mult, p.qk_rnd, p.qk_sh);
-                        else sc = rrs_masked((int32_t)(acc[u] * p.qk_mult), p);
+                        if constexpr (FAST) sc = score_fast(a[u], p.qk_mult, p.qk_rnd, p.qk_sh);
+                        else sc = rrs_masked((int32_t)(a[u] * p.qk_mult), p);
                         sc = clampi(sc, -32768, 32767);
                         // int16 wrap of -(s - rowmax1), clamped to the zero entry
                         const uint32_t idx = min((uint32_t)(rmax1 - sc) & 0xFFFFu, t1);
                         const uint32_t e = u < valid ? (uint32_t)sTab[idx] : 0u;
-                        rsum += (int32_t)e;
+                        rs += (int32_t)e;
                         if ((u & 3) == 0) w4[u >> 2] = e;
                         else w4[u >> 2] |= e << (8 * (u & 3));
                     }
                 }
+            };
+            // ---- pass 2: exp, row sum, P to shared memory ----------------------
+            int32_t rsum = 0;
+            for (int j = 0; j < nkb; ++j) {
+                if (!wait_all(&s_full[sb], sph)) break;
+                tc_fence_after();
+                uint32_t acc[HALVES][32];
+                uint32_t w4[HALVES][8];
+                // half 0 first; the other halves load while it is computed
+                ld_half(sb, 0, acc[0]);
+                tmem_ld_wait();
+#pragma unroll
+                for (int hf = 1; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
+                exp_half(acc[0], T - (j * BK + slice * SC), w4[0], rsum);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[sb]);
+#pragma unroll
+                for (int hf = 1; hf < HALVES; ++hf) exp_half(acc[hf], T - (j * BK + slice * SC + hf * 32), w4[hf], rsum);
                 // the P buffer must be free (P.V of block j-2 done)
                 if (!wait_all(&p_empty[pb], pph ^ 1)) break;
-                // two 16-byte chunks of this row; 128-byte swizzle: chunk k of
+                // 16-byte chunks of this row; 128-byte swizzle: chunk k of
                 // row r lives at chunk (k ^ (r & 7))
                 uint8_t *prow = sP + pb * P_BYTES + r * 128;
-                const int ch0 = slice * 2;
-                *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) = make_uint4(w4[4], w4[5], w4[6], w4[7]);
+#pragma unroll
+                for (int hf = 0; hf < HALVES; ++hf) {
+                    const int ch0 = slice * (SC / 16) + hf * 2;
+                    *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) =
+                        make_uint4(w4[hf][0], w4[hf][1], w4[hf][2], w4[hf][3]);
+                    *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) =
+                        make_uint4(w4[hf][4], w4[hf][5], w4[hf][6], w4[hf][7]);
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[pb]);
@@ -416,12 +458,19 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             // combine row sums
             sRed[slice * BQ + r] = rsum;
             bar_soft();
-            rsum = sRed[r] + sRed[BQ + r] + sRed[2 * BQ + r] + sRed[3 * BQ + r];
+            rsum = 0;
+#pragma unroll
+            for (int sl = 0; sl < SLICES; ++sl) rsum += sRed[sl * BQ + r];
             // ---- epilogue: O / normalise / AV requant ---------------------------
             if (wait_all(&o_full[ob], oph)) {
                 tc_fence_after();
-                uint32_t acc[16];
-                tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * 16), acc);
+                uint32_t acc[OC];
+                if constexpr (OC == 32)
+                    tmem_ld_32x32b_x32(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                                       *reinterpret_cast<uint32_t (*)[32]>(acc));
+                else
+                    tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                                       *reinterpret_cast<uint32_t (*)[16]>(acc));
                 tmem_ld_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -429,9 +478,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                 const int q = q0 + r;
                 if (q < T) {
                     const int32_t inv = fisr(rsum, p.rsqrt_offset);
-                    uint32_t w4[4];
+                    uint32_t w4[OC / 4];
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) {
+                    for (int u = 0; u < OC; ++u) {
                         int32_t v = rrs(wmul((int32_t)acc[u], inv), p.rsqrt_offset);
                         v = rrs(wmul(v, inv), p.rsqrt_offset);
                         v = rrs(wmul(v, (int32_t)p.av_mult), p.av_shift);
@@ -439,8 +488,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         if ((u & 3) == 0) w4[u >> 2] = 0;
                         w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
                     }
-                    int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * 16;
-                    *reinterpret_cast<uint4 *>(o) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * OC;
+#pragma unroll
+                    for (int c4 = 0; c4 < OC / 16; ++c4)
+                        *reinterpret_cast<uint4 *>(o + 16 * c4) =
+                            make_uint4(w4[4 * c4], w4[4 * c4 + 1], w4[4 * c4 + 2], w4[4 * c4 + 3]);
                 }
             }
             if (++ob == 2) { ob = 0; oph ^= 1; }
