@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (uint32_t i = et; i <= t1; i += SOFT_WARPS * 32) sTab[i] = p.tab[2 + i];
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t col = (uint32_t)(slice * SC);
+        const RrsK k_rsq = rrs_k(p.rsqrt_offset), k_av = rrs_k(p.av_shift);  // output normalisation shifts
         int sb = 0, pb = 0, ob = 0;
         uint32_t sph = 0, pph = 0, oph = 0;
         // wait helper: every lane waits (the warp stays converged, which
@@ -481,9 +482,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     uint32_t w4[OC / 4];
 #pragma unroll
                     for (int u = 0; u < OC; ++u) {
-                        int32_t v = rrs(wmul((int32_t)acc[u], inv), p.rsqrt_offset);
-                        v = rrs(wmul(v, inv), p.rsqrt_offset);
-                        v = rrs(wmul(v, (int32_t)p.av_mult), p.av_shift);
+                        int32_t v = rrs_apply(wmul((int32_t)acc[u], inv), k_rsq);
+                        v = rrs_apply(wmul(v, inv), k_rsq);
+                        v = rrs_apply(wmul(v, (int32_t)p.av_mult), k_av);
                         v = clampi(v, -127, 127);
                         if ((u & 3) == 0) w4[u >> 2] = 0;
                         w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));

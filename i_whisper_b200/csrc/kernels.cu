@@ -183,9 +183,12 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const int16_t *__restric
                 t = wadd(wadd(t, kn.rnd), t >> 31) >> kn.sh;
                 t = clampi(t, -16383, 16383);
                 t = wadd(wmul(t, (int32_t)gg[u]), be[u]);
-                t = __mulhi(t, (int32_t)p.out_mult);
-                t = wadd(wadd(t, ko.rnd), t >> 31) >> ko.sh;
-                t = clampi(t, -127, 127);
+                // rrs(mulh(t, m), sh) for m < 2^31: hi(t*m) has the sign of t,
+                // so the rounding and its sign correction are multiply-adds
+                int32_t hq;
+                asm("mad.hi.s32 %0, %1, %2, %3;" : "=r"(hq) : "r"(t), "r"((int32_t)p.out_mult), "r"(ko.rnd));
+                asm("mad.hi.s32 %0, %1, 1, %0;" : "+r"(hq) : "r"(t));
+                t = clampi(hq >> ko.sh, -127, 127);
                 osum += t;
                 packed |= (uint32_t)(uint8_t)t << (8 * u);
             }
