@@ -239,18 +239,24 @@ def int8_mm_peak(torch):
 
 
 # DRAM bytes per launch of the four encoder-layer GEMMs (QKV, out-proj,
-# fc1, fc2) of whisper-medium measured with ncu at M = 48000 rows
-# (profiles/gemm_encoder_dram_traffic.md).
-GEMM_TRAFFIC_M48000 = (148.7e6, 206.8e6, 201.4e6, 373.8e6)
+# fc1, fc2) of whisper-medium measured with ncu at M = 48000 rows, and of
+# the tensor-core attention at 64 windows (profiles/gemm_encoder_dram_traffic.md).
+GEMM_TRAFFIC_M48000 = (149.0e6, 214.1e6, 199.6e6, 376.9e6)
+ATTN_TRAFFIC_B64 = 375.2e6
 
 
-def gemm_traffic_per_launch(windows: int, dims):
-    """Mean DRAM traffic of one encoder GEMM launch at this batch: the
-    measured per-shape bytes scaled by rows (medium only; None otherwise)."""
+def traffic_per_launch(kernel: str, windows: int, dims):
+    """Measured DRAM traffic of one launch of the dominant kernel family at
+    this batch (GEMM: the mean over the four layer shapes, scaled by rows;
+    attention: scaled by windows); medium only, None otherwise."""
     if dims.n_audio_state != 1024:
         return None
-    rows = windows * dims.n_audio_ctx
-    return round(sum(GEMM_TRAFFIC_M48000) / 4 * rows / 48000)
+    if kernel == "attention":
+        return round(ATTN_TRAFFIC_B64 * windows / 64)
+    if kernel == "gemm_i8":
+        rows = windows * dims.n_audio_ctx
+        return round(sum(GEMM_TRAFFIC_M48000) / 4 * rows / 48000)
+    return None
 
 
 def measured_peaks():
@@ -390,9 +396,10 @@ def main():
                 "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4),
                 "peak_source": "measured torch._int_mm int8 8192^3 burst on this GPU (no INT8 entry in MEASURED_PEAKS.json)",
                 "frac_of_datasheet_4500": round(achieved / DATASHEET_INT8_TOPS, 4),
-                "traffic": gemm_traffic_per_launch(B, dims), "traffic_unit": "bytes per launch",
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the four encoder GEMM "
-                                  "shapes at M=48000, scaled by rows (profiles/gemm_encoder_dram_traffic.md)",
+                "traffic": traffic_per_launch(dname, B, dims), "traffic_unit": "bytes per launch",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel family "
+                                  "(GEMM: four encoder shapes at M=48000, scaled by rows; attention: 64 "
+                                  "windows, scaled by windows), profiles/gemm_encoder_dram_traffic.md",
                 "algorithmic_ops_per_launch": dk["ops"] / dk["launches"]}
     else:
         achieved = dk["bytes"] / dk["launches"] / (dk["ms"] / dk["launches"] * 1e-3) / 1e9
