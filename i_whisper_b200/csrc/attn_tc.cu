@@ -19,6 +19,11 @@
 // The reference's online order (row max first, then exp and sum) is kept
 // exactly; no rescaling of partial sums is needed.
 //
+// Each CTA walks its work items in phases: phase ph interleaves, block by
+// block, pass 2 of its item ph-1 with pass 1 of its item ph. Producer, Q.K^T
+// issuer and softmax warps follow that one order through the shared rings
+// (K, S), the P.V issuer takes the pass-2 blocks in item order.
+//
 // Warp roles: warp 0 TMA producer (Q once, K blocks twice, V^T blocks),
 // warp 1 TMEM owner + P.V issuer, warp 18 Q.K^T issuer, warps 2..17 softmax
 // (thread = query row of its TMEM lane quadrant, four warps per quadrant
@@ -63,8 +68,8 @@ constexpr int OFF_Q = 0;                          // two Q buffers
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
-constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // [SLICES][BQ] int32 cross-warp row reductions
-constexpr int OFF_BAR = OFF_RED + 4 * BQ * 4;
+constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // 2 x [SLICES][BQ] int32 cross-warp row max / sum
+constexpr int OFF_BAR = OFF_RED + 2 * SLICES * BQ * 4;
 constexpr int SMEM = 1024 + OFF_BAR + 512;
 constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
 constexpr uint32_t TMEM_O = 384;
@@ -158,6 +163,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     const int nqb = (T + BQ - 1) / BQ;
     const int nkb = (T + BK - 1) / BK;
     const int items = p.B * H * nqb;
+    // work items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ... (grid <= items)
+    const int n_my = ((int)blockIdx.x < items) ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; ++s) {
@@ -194,25 +201,35 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             int qs = 0, ks = 0, vs = 0;
             uint32_t qph = 0, kph = 0, vph = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
-                const int qb = it % nqb, bh = it / nqb;
-                const int h = bh % H, row0 = (bh / H) * T;
-                if (!mbar_wait(&q_empty[qs], qph ^ 1)) { ok = false; break; }
-                mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
-                tma_load_2d(&tmQ, &q_full[qs], sQ + qs * Q_BYTES, h * 64, row0 + qb * BQ);
-                if (++qs == 2) { qs = 0; qph ^= 1; }
-                for (int pass = 0; pass < 2 && ok; ++pass) {
-                    for (int j = 0; j < nkb; ++j) {
+            // Phase ph interleaves pass 2 of this CTA's item ph-1 with pass 1
+            // of its item ph (block by block), the order every role follows.
+            for (int ph = 0; ph <= n_my && ok && !*abort_flag; ++ph) {
+                const bool has1 = ph < n_my, has2 = ph > 0;
+                const int it1 = blockIdx.x + ph * gridDim.x, it2 = it1 - gridDim.x;
+                const int bh1 = it1 / nqb, bh2 = it2 / nqb;
+                const int h1 = bh1 % H, row1 = (bh1 / H) * T, h2 = bh2 % H, row2 = (bh2 / H) * T;
+                if (has1) {
+                    if (!mbar_wait(&q_empty[qs], qph ^ 1)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
+                    tma_load_2d(&tmQ, &q_full[qs], sQ + qs * Q_BYTES, h1 * 64, row1 + (it1 % nqb) * BQ);
+                    if (++qs == 2) { qs = 0; qph ^= 1; }
+                }
+                for (int j = 0; j < nkb && ok; ++j) {
+                    if (has2) {
                         if (!mbar_wait(&k_empty[ks], kph ^ 1)) { ok = false; break; }
                         mbar_arrive_expect_tx(&k_full[ks], K_BYTES);
-                        tma_load_2d(&tmK, &k_full[ks], sK + ks * K_BYTES, h * 64, row0 + j * BK);
+                        tma_load_2d(&tmK, &k_full[ks], sK + ks * K_BYTES, h2 * 64, row2 + j * BK);
                         if (++ks == KST) { ks = 0; kph ^= 1; }
-                        if (pass == 1) {
-                            if (!mbar_wait(&v_empty[vs], vph ^ 1)) { ok = false; break; }
-                            mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
-                            tma_load_2d(&tmV, &v_full[vs], sV + vs * V_BYTES, j * BK, bh * 64);
-                            if (++vs == VST) { vs = 0; vph ^= 1; }
-                        }
+                        if (!mbar_wait(&v_empty[vs], vph ^ 1)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&v_full[vs], V_BYTES);
+                        tma_load_2d(&tmV, &v_full[vs], sV + vs * V_BYTES, j * BK, bh2 * 64);
+                        if (++vs == VST) { vs = 0; vph ^= 1; }
+                    }
+                    if (has1) {
+                        if (!mbar_wait(&k_empty[ks], kph ^ 1)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&k_full[ks], K_BYTES);
+                        tma_load_2d(&tmK, &k_full[ks], sK + ks * K_BYTES, h1 * 64, row1 + j * BK);
+                        if (++ks == KST) { ks = 0; kph ^= 1; }
                     }
                 }
             }
@@ -226,33 +243,37 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             bool ok = true;
             if (warp == QK_WARP) {
                 constexpr uint32_t idesc_qk = idesc_i8(BQ, BK, true, true);
-                int qs = 0, ks = 0, sb = 0;
-                uint32_t qph = 0, kph = 0, sph = 0;
-                for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
-                    if (!mbar_wait(&q_full[qs], qph)) { ok = false; break; }
+                int ks = 0, sb = 0;
+                uint32_t kph = 0, sph = 0;
+                // item k of this CTA uses Q buffer k & 1, q_full phase (k >> 1) & 1
+                auto issue_qk = [&](int k) -> bool {
+                    if (!mbar_wait(&s_empty[sb], sph ^ 1) || !mbar_wait(&k_full[ks], kph)) return false;
                     tc_fence_after();
-                    const uint32_t qa = smem_u32(sQ + qs * Q_BYTES);
-                    for (int pass = 0; pass < 2 && ok; ++pass) {
-                        for (int j = 0; j < nkb; ++j) {
-                            if (!mbar_wait(&s_empty[sb], sph ^ 1) || !mbar_wait(&k_full[ks], kph)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                            const uint32_t ka = smem_u32(sK + ks * K_BYTES);
-                            const uint32_t d = tmem_base + (uint32_t)(sb * BK);
+                    const uint32_t qa = smem_u32(sQ + (k & 1) * Q_BYTES);
+                    const uint32_t ka = smem_u32(sK + ks * K_BYTES);
+                    const uint32_t d = tmem_base + (uint32_t)(sb * BK);
 #pragma unroll
-                            for (int kk = 0; kk < 2; ++kk)
-                                mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
-                            mma_commit(&k_empty[ks]);
-                            mma_commit(&s_full[sb]);
-                            if (++ks == KST) { ks = 0; kph ^= 1; }
-                            if (++sb == SBUF) { sb = 0; sph ^= 1; }
-                        }
+                    for (int kk = 0; kk < 2; ++kk)
+                        mma_i8(d, sdesc_kmajor_sw64(qa + kk * 32), sdesc_kmajor_sw64(ka + kk * 32), idesc_qk, kk);
+                    mma_commit(&k_empty[ks]);
+                    mma_commit(&s_full[sb]);
+                    if (++ks == KST) { ks = 0; kph ^= 1; }
+                    if (++sb == SBUF) { sb = 0; sph ^= 1; }
+                    return true;
+                };
+                for (int ph = 0; ph <= n_my && ok && !*abort_flag; ++ph) {
+                    const bool has1 = ph < n_my, has2 = ph > 0;
+                    if (has1) {
+                        if (!mbar_wait(&q_full[ph & 1], (uint32_t)(ph >> 1) & 1u)) { ok = false; break; }
+                        tc_fence_after();
                     }
-                    if (!ok) break;
-                    mma_commit(&q_empty[qs]);  // every QK of this item issued
-                    if (++qs == 2) { qs = 0; qph ^= 1; }
+                    for (int j = 0; j < nkb && ok; ++j) {
+                        if (has2) {
+                            if (!issue_qk(ph - 1)) { ok = false; break; }
+                            if (j + 1 == nkb) mma_commit(&q_empty[(ph - 1) & 1]);  // item ph-1's last QK issued
+                        }
+                        if (has1 && !issue_qk(ph)) { ok = false; break; }
+                    }
                 }
             } else {
                 constexpr uint32_t idesc_pv = idesc_i8(BQ, 64, false, true);
@@ -323,180 +344,195 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         auto ld_half = [&](int sbuf, int hf, uint32_t (&a)[32]) {
             tmem_ld_32x32b_x32(tmem_base + lane_base + (uint32_t)(sbuf * BK) + col + (uint32_t)(hf * 32), a);
         };
-        for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        // Pass-2 state of the item whose pass 1 ended in the previous phase.
+        int32_t rmax1 = 0;
+        bool warp_simple = false;
+        uint32_t cidx = 0;
+        const uint32_t negm = 0u - p.qk_mult;
+        // exp of 32 scores of one half into eight packed words, adding to rs
+        auto exp_half = [&](const uint32_t (&a)[32], int valid, uint32_t (&w4)[8], int32_t &rs) {
+            if (FAST && warp_simple && valid >= 32) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                    uint32_t ww = 0;
+#pragma unroll
+                    for (int k4 = 0; k4 < 4; ++k4) {
+                        const uint32_t idx = min(exp_index(a[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
+                        // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
+                        asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
+                    }
+                    rs = __dp4a((int32_t)ww, 0x01010101, rs);
+                    w4[q4] = ww;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    int32_t sc;
+                    if constexpr (FAST) sc = score_fast(a[u], p.qk_mult, p.qk_rnd, p.qk_sh);
+                    else sc = rrs_masked((int32_t)(a[u] * p.qk_mult), p);
+                    sc = clampi(sc, -32768, 32767);
+                    // int16 wrap of -(s - rowmax1), clamped to the zero entry
+                    const uint32_t idx = min((uint32_t)(rmax1 - sc) & 0xFFFFu, t1);
+                    const uint32_t e = u < valid ? (uint32_t)sTab[idx] : 0u;
+                    rs += (int32_t)e;
+                    if ((u & 3) == 0) w4[u >> 2] = e;
+                    else w4[u >> 2] |= e << (8 * (u & 3));
+                }
+            }
+        };
+        int32_t *sRedMax = sRed, *sRedSum = sRed + SLICES * BQ;
+        // Phase ph: pass 2 of this CTA's item ph-1 block by block interleaved
+        // with pass 1 of its item ph, so that the light pass-1 blocks (a row
+        // max) fill the Q.K^T round trip that the heavy pass-2 blocks hide.
+        for (int ph = 0; ph <= n_my; ++ph) {
             // every softmax warp reads the abort flag between the same two
             // barriers (it is only written outside them) and leaves together
             bar_soft();
             const bool stop = *abort_flag != 0;
             bar_soft();
             if (stop) break;
-            const int qb = it % nqb, bh = it / nqb;
-            const int h = bh % H, row0 = (bh / H) * T;
-            const int q0 = qb * BQ;
-            // ---- pass 1: raw row max ------------------------------------------
-            int32_t mx = INT32_MIN;
+            const bool has1 = ph < n_my, has2 = ph > 0;
+            const int it2 = (int)blockIdx.x + (ph - 1) * (int)gridDim.x;
+            int32_t mx = INT32_MIN, rsum = 0;
             for (int j = 0; j < nkb; ++j) {
-                if (!wait_all(&s_full[sb], sph)) break;
-                tc_fence_after();
-                uint32_t acc[HALVES][32];
+                if (has2) {
+                    // ---- pass 2 of item ph-1: exp, row sum, P to shared memory
+                    if (!wait_all(&s_full[sb], sph)) break;
+                    tc_fence_after();
+                    uint32_t acc[HALVES][32];
+                    uint32_t w4[HALVES][8];
+                    // half 0 first; the other halves load while it is computed
+                    ld_half(sb, 0, acc[0]);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int hf = 0; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[sb]);  // S is in registers: release it early
+                    for (int hf = 1; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
+                    exp_half(acc[0], T - (j * BK + slice * SC), w4[0], rsum);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_empty[sb]);
 #pragma unroll
-                for (int hf = 0; hf < HALVES; ++hf) {
-                    const int valid = T - (j * BK + slice * SC + hf * 32);
-                    if (valid >= 32) {
+                    for (int hf = 1; hf < HALVES; ++hf)
+                        exp_half(acc[hf], T - (j * BK + slice * SC + hf * 32), w4[hf], rsum);
+                    // the P buffer must be free (P.V of block j-2 done)
+                    if (!wait_all(&p_empty[pb], pph ^ 1)) break;
+                    // 16-byte chunks of this row; 128-byte swizzle: chunk k of
+                    // row r lives at chunk (k ^ (r & 7))
+                    uint8_t *prow = sP + pb * P_BYTES + r * 128;
 #pragma unroll
-                        for (int u = 0; u < 32; ++u) mx = max(mx, (int32_t)acc[hf][u]);
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < 32; ++u)
-                            if (u < valid) mx = max(mx, (int32_t)acc[hf][u]);
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        const int ch0 = slice * (SC / 16) + hf * 2;
+                        *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) =
+                            make_uint4(w4[hf][0], w4[hf][1], w4[hf][2], w4[hf][3]);
+                        *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) =
+                            make_uint4(w4[hf][4], w4[hf][5], w4[hf][6], w4[hf][7]);
                     }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p_full[pb]);
+                    if (++sb == SBUF) { sb = 0; sph ^= 1; }
+                    if (++pb == 2) { pb = 0; pph ^= 1; }
                 }
-                if (++sb == SBUF) { sb = 0; sph ^= 1; }
-            }
-            // combine the column slices of each row
-            sRed[slice * BQ + r] = mx;
-            bar_soft();
+                if (has1) {
+                    // ---- pass 1 of item ph: raw row max
+                    if (!wait_all(&s_full[sb], sph)) break;
+                    tc_fence_after();
+                    uint32_t acc[HALVES][32];
 #pragma unroll
-            for (int sl = 0; sl < SLICES; ++sl) mx = max(mx, sRed[sl * BQ + r]);
-            bar_soft();
-            // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
-            const int32_t sraw = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
-            const int32_t smax = clampi(sraw, -32768, 32767);
-            const int32_t rmax1 = (int32_t)(int16_t)(smax + 1);
-            // For a row whose requantised max is below 32767 (no int16 wrap of
-            // rowmax+1) and whose rowmax1 + 32768 >= t1, neither the int16 clamp
-            // of a score nor the int16 wrap of its difference can change the
-            // table index: idx = min(rowmax1 - s, t1) with s unclamped. The warp
-            // uses that path only when all of its 32 rows qualify.
-            // On that path the index is computed from the raw score in two
-            // multiply-adds: with y = acc*m + rnd - [acc < 0] (the rounding
-            // shift's numerator, |acc*m| < 2^28) and the row's unclamped
-            // requantised max rowmax1 - 1 = y_max >> sh,
-            //   rowmax1 - (y >> sh) = (C - acc*m + [acc < 0]) >> sh,
-            //   C = (rowmax1 + 1) * 2^sh - 1 - rnd,
-            // where the numerator lies in [2^sh, 2^29 + 2^(sh+1)) and so is
-            // exact in unsigned 32-bit arithmetic for sh <= 30.
-            const bool warp_simple =
-                __all_sync(0xffffffffu, sraw > -32768 && sraw < 32767 && rmax1 + 32768 >= (int32_t)t1) &&
-                p.qk_sh <= 30;
-            const uint32_t cidx = ((uint32_t)(rmax1 + 1) << p.qk_sh) - 1u - p.qk_rnd;
-            const uint32_t negm = 0u - p.qk_mult;
-            // exp of 32 scores of one half into eight packed words, adding to rsum
-            auto exp_half = [&](const uint32_t (&a)[32], int valid, uint32_t (&w4)[8], int32_t &rs) {
-                if (FAST && warp_simple && valid >= 32) {
+                    for (int hf = 0; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_empty[sb]);  // S is in registers: release it early
 #pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        uint32_t ww = 0;
+                    for (int hf = 0; hf < HALVES; ++hf) {
+                        const int valid = T - (j * BK + slice * SC + hf * 32);
+                        if (valid >= 32) {
 #pragma unroll
-                        for (int k4 = 0; k4 < 4; ++k4) {
-                            const uint32_t idx = min(exp_index(a[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
-                            // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
-                            asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
+                            for (int u = 0; u < 32; ++u) mx = max(mx, (int32_t)acc[hf][u]);
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 32; ++u)
+                                if (u < valid) mx = max(mx, (int32_t)acc[hf][u]);
                         }
-                        rs = __dp4a((int32_t)ww, 0x01010101, rs);
-                        w4[q4] = ww;
                     }
-                } else {
-#pragma unroll
-                    for (int u = 0; u < 32; ++u) {
-                        int32_t sc;
-                        if constexpr (FAST) sc = score_fast(a[u], p.qk_mult, p.qk_rnd, p.qk_sh);
-                        else sc = rrs_masked((int32_t)(a[u] * p.qk_mult), p);
-                        sc = clampi(sc, -32768, 32767);
-                        // int16 wrap of -(s - rowmax1), clamped to the zero entry
-                        const uint32_t idx = min((uint32_t)(rmax1 - sc) & 0xFFFFu, t1);
-                        const uint32_t e = u < valid ? (uint32_t)sTab[idx] : 0u;
-                        rs += (int32_t)e;
-                        if ((u & 3) == 0) w4[u >> 2] = e;
-                        else w4[u >> 2] |= e << (8 * (u & 3));
-                    }
-                }
-            };
-            // ---- pass 2: exp, row sum, P to shared memory ----------------------
-            int32_t rsum = 0;
-            for (int j = 0; j < nkb; ++j) {
-                if (!wait_all(&s_full[sb], sph)) break;
-                tc_fence_after();
-                uint32_t acc[HALVES][32];
-                uint32_t w4[HALVES][8];
-                // half 0 first; the other halves load while it is computed
-                ld_half(sb, 0, acc[0]);
-                tmem_ld_wait();
-#pragma unroll
-                for (int hf = 1; hf < HALVES; ++hf) ld_half(sb, hf, acc[hf]);
-                exp_half(acc[0], T - (j * BK + slice * SC), w4[0], rsum);
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[sb]);
-#pragma unroll
-                for (int hf = 1; hf < HALVES; ++hf) exp_half(acc[hf], T - (j * BK + slice * SC + hf * 32), w4[hf], rsum);
-                // the P buffer must be free (P.V of block j-2 done)
-                if (!wait_all(&p_empty[pb], pph ^ 1)) break;
-                // 16-byte chunks of this row; 128-byte swizzle: chunk k of
-                // row r lives at chunk (k ^ (r & 7))
-                uint8_t *prow = sP + pb * P_BYTES + r * 128;
-#pragma unroll
-                for (int hf = 0; hf < HALVES; ++hf) {
-                    const int ch0 = slice * (SC / 16) + hf * 2;
-                    *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) =
-                        make_uint4(w4[hf][0], w4[hf][1], w4[hf][2], w4[hf][3]);
-                    *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) =
-                        make_uint4(w4[hf][4], w4[hf][5], w4[hf][6], w4[hf][7]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[pb]);
-                if (++sb == SBUF) { sb = 0; sph ^= 1; }
-                if (++pb == 2) { pb = 0; pph ^= 1; }
-            }
-            // combine row sums
-            sRed[slice * BQ + r] = rsum;
-            bar_soft();
-            rsum = 0;
-#pragma unroll
-            for (int sl = 0; sl < SLICES; ++sl) rsum += sRed[sl * BQ + r];
-            // ---- epilogue: O / normalise / AV requant ---------------------------
-            if (wait_all(&o_full[ob], oph)) {
-                tc_fence_after();
-                uint32_t acc[OC];
-                if constexpr (OC == 32)
-                    tmem_ld_32x32b_x32(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
-                                       *reinterpret_cast<uint32_t (*)[32]>(acc));
-                else
-                    tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
-                                       *reinterpret_cast<uint32_t (*)[16]>(acc));
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&o_empty[ob]);
-                const int q = q0 + r;
-                if (q < T) {
-                    const int32_t inv = fisr(rsum, p.rsqrt_offset);
-                    uint32_t w4[OC / 4];
-#pragma unroll
-                    for (int u = 0; u < OC; ++u) {
-                        int32_t v = rrs_apply(wmul((int32_t)acc[u], inv), k_rsq);
-                        v = rrs_apply(wmul(v, inv), k_rsq);
-                        v = rrs_apply(wmul(v, (int32_t)p.av_mult), k_av);
-                        v = clampi(v, -127, 127);
-                        if ((u & 3) == 0) w4[u >> 2] = 0;
-                        w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
-                    }
-                    int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * OC;
-#pragma unroll
-                    for (int c4 = 0; c4 < OC / 16; ++c4)
-                        *reinterpret_cast<uint4 *>(o + 16 * c4) =
-                            make_uint4(w4[4 * c4], w4[4 * c4 + 1], w4[4 * c4 + 2], w4[4 * c4 + 3]);
+                    if (++sb == SBUF) { sb = 0; sph ^= 1; }
                 }
             }
-            if (++ob == 2) { ob = 0; oph ^= 1; }
+            if (has2) {
+                // combine row sums
+                sRedSum[slice * BQ + r] = rsum;
+                bar_soft();
+                rsum = 0;
+#pragma unroll
+                for (int sl = 0; sl < SLICES; ++sl) rsum += sRedSum[sl * BQ + r];
+                // ---- epilogue of item ph-1: O / normalise / AV requant ---------
+                const int qb = it2 % nqb, bh = it2 / nqb;
+                const int h = bh % H, row0 = (bh / H) * T;
+                const int q0 = qb * BQ;
+                if (wait_all(&o_full[ob], oph)) {
+                    tc_fence_after();
+                    uint32_t acc[OC];
+                    if constexpr (OC == 32)
+                        tmem_ld_32x32b_x32(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                                           *reinterpret_cast<uint32_t (*)[32]>(acc));
+                    else
+                        tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                                           *reinterpret_cast<uint32_t (*)[16]>(acc));
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_empty[ob]);
+                    const int q = q0 + r;
+                    if (q < T) {
+                        const int32_t inv = fisr(rsum, p.rsqrt_offset);
+                        uint32_t w4[OC / 4];
+#pragma unroll
+                        for (int u = 0; u < OC; ++u) {
+                            int32_t v = rrs_apply(wmul((int32_t)acc[u], inv), k_rsq);
+                            v = rrs_apply(wmul(v, inv), k_rsq);
+                            v = rrs_apply(wmul(v, (int32_t)p.av_mult), k_av);
+                            v = clampi(v, -127, 127);
+                            if ((u & 3) == 0) w4[u >> 2] = 0;
+                            w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                        }
+                        int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * OC;
+#pragma unroll
+                        for (int c4 = 0; c4 < OC / 16; ++c4)
+                            *reinterpret_cast<uint4 *>(o + 16 * c4) =
+                                make_uint4(w4[4 * c4], w4[4 * c4 + 1], w4[4 * c4 + 2], w4[4 * c4 + 3]);
+                    }
+                }
+                if (++ob == 2) { ob = 0; oph ^= 1; }
+            }
+            if (has1) {
+                // combine the column slices of each row
+                sRedMax[slice * BQ + r] = mx;
+                bar_soft();
+#pragma unroll
+                for (int sl = 0; sl < SLICES; ++sl) mx = max(mx, sRedMax[sl * BQ + r]);
+                // requantised row max + 1 (int16 wrap), qk_requant_rowmax_scalar
+                const int32_t sraw = rrs_masked((int32_t)((uint32_t)mx * p.qk_mult), p);
+                const int32_t smax = clampi(sraw, -32768, 32767);
+                rmax1 = (int32_t)(int16_t)(smax + 1);
+                // For a row whose requantised max is below 32767 (no int16 wrap
+                // of rowmax+1) and whose rowmax1 + 32768 >= t1, neither the int16
+                // clamp of a score nor the int16 wrap of its difference can
+                // change the table index: idx = min(rowmax1 - s, t1) with s
+                // unclamped. The warp uses that path only when all of its 32
+                // rows qualify. On that path the index is computed from the raw
+                // score in two multiply-adds: with y = acc*m + rnd - [acc < 0]
+                // (the rounding shift's numerator, |acc*m| < 2^28) and the
+                // row's unclamped requantised max rowmax1 - 1 = y_max >> sh,
+                //   rowmax1 - (y >> sh) = (C - acc*m + [acc < 0]) >> sh,
+                //   C = (rowmax1 + 1) * 2^sh - 1 - rnd,
+                // where the numerator lies in [2^sh, 2^29 + 2^(sh+1)) and so is
+                // exact in unsigned 32-bit arithmetic for sh <= 30.
+                warp_simple =
+                    __all_sync(0xffffffffu, sraw > -32768 && sraw < 32767 && rmax1 + 32768 >= (int32_t)t1) &&
+                    p.qk_sh <= 30;
+                cidx = ((uint32_t)(rmax1 + 1) << p.qk_sh) - 1u - p.qk_rnd;
+            }
         }
     }
     tc_fence_before();
