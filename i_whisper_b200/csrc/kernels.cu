@@ -223,9 +223,10 @@ cudaError_t layernorm32(const int16_t *x, int64_t ldx, const int8_t *gamma, cons
     if ((reinterpret_cast<uintptr_t>(x) & 7) || (ldx & 3) || (reinterpret_cast<uintptr_t>(y) & 3) || (ldy & 3) ||
         (reinterpret_cast<uintptr_t>(gamma) & 3) || (beta && (reinterpret_cast<uintptr_t>(beta) & 15)))
         return cudaErrorMisalignedAddress;
-    // one warp per row; few rows (decode steps) get 4-warp CTAs so that they
-    // spread over more SMs with one warp per sub-partition
-    const int threads = rows < 8192 ? 128 : 256;
+    // one warp per row in 4-warp CTAs: decode-sized row counts spread over
+    // more SMs with one warp per sub-partition, and encoder-sized ones
+    // measured 2.6% faster than with 8-warp CTAs
+    const int threads = 128;
     const int blocks = (rows * 32 + threads - 1) / threads;
 #define IW_LN_CASE(DD)                                                                                        \
     case DD:                                                                                                  \
