@@ -53,6 +53,8 @@ SIGNATURES = {
     "iw_attention_ex": [_P, _P],
     "iw_layernorm32_ex": [_P, _I64, _P, _P, _U8, _I8, _U32, _I8, _P, _I64, _I64, _I64, _P, _P, _P],
     "iw_im2col": [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P],
+    "iw_channels_last_pad": [_P, _I64, _I64, _I64, _I64, _I64, _P, _P],
+    "iw_zero_rows": [_P, _I64, _I64, _I64, _P],
     "iw_embed_add_requant15_dev": [_P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "iw_kv_append": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "iw_greedy_step": [_P, _I64, _P],
@@ -84,6 +86,7 @@ class GemmDesc(C.Structure):
         ("vt_out", _P), ("vt_ld", _I64), ("vt_col0", _I64), ("vt_T", _I64),
         ("kv_cache_k", _P), ("kv_cache_v", _P), ("kv_col0", _I64), ("kv_heads", _I64), ("kv_T", _I64),
         ("kv_Tcap", _I64), ("kv_pos", _I64), ("kv_pos_dev", _P), ("gelu_table_tiled", _P),
+        ("x_window_rows", _I64), ("x_window_stride", _I64),
     ]
 
 

@@ -472,6 +472,15 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     if (d->gelu_table && (d->lut || d->mode != IW_GEMM_INT8 || !d->multiplier))
         return fail(IW_EINVAL, "iw_gemm_i8: gelu_table needs a per-channel int8 epilogue without lut");
     iw::GemmShape g{d->x, d->ldx, d->w, d->ldw, (int)d->M, (int)d->N, (int)d->K};
+    if (d->x_window_rows) {
+        if (d->x_window_rows < 0 || d->M % d->x_window_rows || d->x_window_stride < 0 || d->x_window_stride % 16 ||
+            d->x_window_rows > INT32_MAX || !iw::cm_enabled() || d->vt_out || d->kv_cache_k || d->headmajor_T ||
+            d->transpose_T)
+            return fail(IW_EINVAL, "iw_gemm_i8: invalid windowed X (rows dividing M, 16-byte window stride, "
+                                   "row-major or positional-add output)");
+        g.win_rows = (int)d->x_window_rows;
+        g.win_stride = d->x_window_stride;
+    }
     return cuda_check(iw::gemm_i8_launch(g, (iw::EpiMode)d->mode, p, S(stream), d->tile_n), "iw_gemm_i8");
 }
 
@@ -603,6 +612,21 @@ int iw_im2col(const int8_t *x, int8_t *out, int64_t B, int64_t Cin, int64_t Tin,
     return cuda_check(iw::im2col(x, out, (int)B, (int)Cin, (int)Tin, (int)K, (int)stride, (int)pad, (int)Tout, ldo,
                                  channels_last, S(stream)),
                       "iw_im2col");
+}
+
+int iw_channels_last_pad(const int8_t *x, int64_t B, int64_t C, int64_t T, int64_t front, int64_t back, int8_t *out,
+                         void *stream) {
+    if (B < 0 || C < 0 || T < 0 || front < 0 || back < 0 || B > 65535 || (T + front + back) > INT32_MAX / 2 ||
+        C > INT32_MAX / 2)
+        return fail(IW_EINVAL, "iw_channels_last_pad: invalid shape");
+    return cuda_check(iw::channels_last_pad(x, (int)B, (int)C, (int)T, (int)front, (int)back, out, S(stream)),
+                      "iw_channels_last_pad");
+}
+
+int iw_zero_rows(void *p, int64_t count, int64_t bytes, int64_t pitch, void *stream) {
+    if (count < 0 || bytes < 0 || pitch < bytes) return fail(IW_EINVAL, "iw_zero_rows: invalid shape");
+    if (count == 0 || bytes == 0) return IW_OK;
+    return cuda_check(cudaMemset2DAsync(p, (size_t)pitch, 0, (size_t)bytes, (size_t)count, S(stream)), "iw_zero_rows");
 }
 
 int iw_embed_add_requant15_dev(const int8_t *table, const int64_t *tokens, const int8_t *pe,

@@ -129,7 +129,7 @@ IW_DEV int32_t gelu_tab_k(int32_t x, const uint8_t *gb) { return (int32_t)gb[x *
 template <int BR, int MODE, int GK>
 __global__ void __launch_bounds__(kCmThreads, 1)
     gemm_cm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N,
-                   int K, const EpiParams p) {
+                   int K, int WR, const EpiParams p) {
     using Cfg = CmCfg<BR, GK>;
     constexpr int S = Cfg::STAGES;
     constexpr bool GT = GK == 2;
@@ -154,7 +154,24 @@ __global__ void __launch_bounds__(kCmThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int ch_tiles = (N + 127) / 128;
-    const int row_tiles = (M + BR - 1) / BR;
+    // WR > 0: X is M/WR windows of WR rows (a 3-D tensor map; rows may
+    // overlap, which reads a channels-last activation as the im2col matrix
+    // of a convolution); row tiles never straddle two windows
+    const int tpw = WR > 0 ? (WR + BR - 1) / BR : 1;
+    const int row_tiles = WR > 0 ? (M / WR) * tpw : (M + BR - 1) / BR;
+    // first output row, row end, window and row within the window of row tile rt
+    auto tile_rows = [&](int rt, int &m0, int &mend, int &wb, int &tw) {
+        if (WR > 0) {
+            wb = rt / tpw;
+            tw = (rt - wb * tpw) * BR;
+            m0 = wb * WR + tw;
+            mend = wb * WR + WR;
+        } else {
+            wb = 0;
+            tw = m0 = rt * BR;
+            mend = M;
+        }
+    };
     const int tiles = ch_tiles * row_tiles;
     const int kblocks = (K + kBlockK - 1) / kBlockK;
     // Row sums of a full row tile come by one bulk copy when 16-byte aligned;
@@ -201,13 +218,14 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             int ab = 0;
             uint32_t aph = 0, aux_issued = 0, aux_parity = 0;
             for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
-                const int m0 = (tile / ch_tiles) * BR;
+                int m0, mend, wb, tw;
+                tile_rows(tile / ch_tiles, m0, mend, wb, tw);
                 const int n0 = (tile % ch_tiles) * 128;
                 {
                     // the tile's epilogue inputs (an empty transaction when
                     // the epilogue warps load them themselves)
                     if (!mbar_wait(&aux_empty[ab], aph ^ 1)) { *abort_flag = 1; break; }
-                    const bool rs_t = rs_bulk && m0 + BR <= M;
+                    const bool rs_t = rs_bulk && m0 + BR <= mend;
                     mbar_arrive_expect_tx(&aux_full[ab], (rs_t ? Cfg::RS_BYTES : 0) + (gt_bulk ? Cfg::GTAB_BYTES : 0));
                     if (rs_t) bulk_load(rs_s + ab * BR, p.rowsum + m0, Cfg::RS_BYTES, &aux_full[ab]);
                     if (gt_bulk)
@@ -221,7 +239,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                     if (!mbar_wait(&empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
                     tma_load_2d(&tmW, &full[stage], sA + stage * Cfg::A_BYTES, kb * kBlockK, n0);
-                    tma_load_2d(&tmX, &full[stage], sB + stage * Cfg::B_BYTES, kb * kBlockK, m0);
+                    if (WR > 0)
+                        tma_load_3d(&tmX, &full[stage], sB + stage * Cfg::B_BYTES, kb * kBlockK, tw, wb);
+                    else
+                        tma_load_2d(&tmX, &full[stage], sB + stage * Cfg::B_BYTES, kb * kBlockK, m0);
                     issued_mask |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) { stage = 0; phase ^= 1; }
@@ -282,7 +303,8 @@ __global__ void __launch_bounds__(kCmThreads, 1)
         int ab = 0;
         uint32_t aph = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int m0 = (tile / ch_tiles) * BR;
+            int m0, Mt, wb_, tw_;
+            tile_rows(tile / ch_tiles, m0, Mt, wb_, tw_);  // rows [m0, min(m0 + BR, Mt))
             const int n0 = (tile % ch_tiles) * 128;
             int32_t *rs_t = rs_s + ab * BR;
             uint32_t *gt_t = gtab_s + ab * 8192;
@@ -291,9 +313,9 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             // epilogue warps take the same decision.
             cm_bar();
             if (et == 0) *stop_s = *abort_flag;
-            if (!(rs_bulk && m0 + BR <= M))
+            if (!(rs_bulk && m0 + BR <= Mt))
                 for (int i = et; i < BR; i += kCmEpiWarps * 32)
-                    rs_t[i] = (p.wz && m0 + i < M) ? __ldg(p.rowsum + m0 + i) : 0;
+                    rs_t[i] = (p.wz && m0 + i < Mt) ? __ldg(p.rowsum + m0 + i) : 0;
             if (GT && !gt_bulk) {
                 // 16 table bytes of one channel per thread, scattered into
                 // the lookup layout (used only without the pre-arranged table)
@@ -341,7 +363,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
 #pragma unroll 1
                 for (int c = slice; c < BR / kCmCh; c += kCmEpiWarps / 4) {
                     const int r0 = m0 + c * kCmCh;
-                    if (r0 >= M) break;  // warp-uniform
+                    if (r0 >= Mt) break;  // warp-uniform
                     uint32_t acc[kCmCh];
                     tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BR + c * kCmCh),
                                        acc);
@@ -400,7 +422,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             int32_t rv[kCmCh];
                             const int16_t *res = p.res + (int64_t)r0 * p.ldr + n;
                             int16_t *o16 = out + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= M && p.ldr < (1 << 26) && p.ldo < (1 << 26)) {
+                            if (r0 + kCmCh <= Mt && p.ldr < (1 << 26) && p.ldo < (1 << 26)) {
                                 // whole chunk: 32-bit row offsets
                                 const uint32_t ldr32 = (uint32_t)p.ldr, ldo32 = (uint32_t)p.ldo;
 #pragma unroll
@@ -414,10 +436,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             } else {
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j)
-                                    rv[j] = (r0 + j < M) ? (int32_t)res[(int64_t)j * p.ldr] : 0;
+                                    rv[j] = (r0 + j < Mt) ? (int32_t)res[(int64_t)j * p.ldr] : 0;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
-                                    if (r0 + j < M) {
+                                    if (r0 + j < Mt) {
                                         int32_t t = u_mad(rv[j], rm, v[j]);
                                         t = u_add(u_add(t, 1 << 14), t >> 31) >> 15;
                                         o16[(int64_t)j * p.ldo] = (int16_t)clampi(t, -16383, 16383);
@@ -446,12 +468,12 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                 int t = r0 % p.pe_T;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
-                                    pe[j] = (r0 + j < M) ? (int32_t)__ldg(p.pe + (int64_t)t * N + n) : 0;
+                                    pe[j] = (r0 + j < Mt) ? (int32_t)__ldg(p.pe + (int64_t)t * N + n) : 0;
                                     if (++t == p.pe_T) t = 0;
                                 }
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
-                                    if (r0 + j < M) {
+                                    if (r0 + j < Mt) {
                                         const int32_t a = clampi(rrs_apply(wmul(v[j] + pe[j], ck.pm), ck.ps), -16383, 16383);
                                         out[(int64_t)(r0 + j) * p.ldo + n] = (int16_t)a;
                                     }
@@ -466,7 +488,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
 #pragma unroll
                                 for (int j = 0; j < kCmCh; j += 4) {
                                     const int m = r0 + j;
-                                    if (vec && m + 3 < M) {
+                                    if (vec && m + 3 < Mt) {
                                         int8_t *dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
                                         *reinterpret_cast<uint32_t *>(dst) =
                                             (uint32_t)(uint8_t)v[j] | ((uint32_t)(uint8_t)v[j + 1] << 8) |
@@ -476,7 +498,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                     } else {
 #pragma unroll
                                         for (int u = 0; u < 4; ++u) {
-                                            if (m + u < M)
+                                            if (m + u < Mt)
                                                 p.tr_out[((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t] =
                                                     (int8_t)v[j + u];
                                             if (++t == p.tr_T) { t = 0; ++b; }
@@ -490,7 +512,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                 int b = r0 / p.kv_T, t = r0 - (r0 / p.kv_T) * p.kv_T;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
-                                    if (r0 + j < M)
+                                    if (r0 + j < Mt)
                                         kv_base[((int64_t)b * p.kv_H * p.kv_Tcap + t) * 64] = (int8_t)v[j];
                                     if (++t == p.kv_T) { t = 0; ++b; }
                                 }
@@ -502,11 +524,11 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                                (n & 63);
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j)
-                                    if (r0 + j < M) base[(int64_t)(r0 + j) * 64] = (int8_t)v[j];
+                                    if (r0 + j < Mt) base[(int64_t)(r0 + j) * 64] = (int8_t)v[j];
                             }
                         } else if (cv) {
                             int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= M && p.ldo < (1 << 27)) {
+                            if (r0 + kCmCh <= Mt && p.ldo < (1 << 27)) {
                                 // 32-bit row offsets: one wide multiply-add per address
                                 const uint32_t ldo32 = (uint32_t)p.ldo;
 #pragma unroll
@@ -514,7 +536,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             } else {
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
-                                    if (r0 + j < M) *out = (int8_t)v[j];
+                                    if (r0 + j < Mt) *out = (int8_t)v[j];
                                     out += p.ldo;
                                 }
                             }
@@ -565,7 +587,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                 // Barrier C: all four quadrants' partial sums of each row are in.
                 cm_bar();
                 for (int i = et; i < BR; i += kCmEpiWarps * 32)
-                    if (m0 + i < M)
+                    if (m0 + i < Mt)
                         atomicAdd(p.rowsum_out + m0 + i, part[i] + part[BR + i] + part[2 * BR + i] + part[3 * BR + i]);
             }
         }
@@ -585,7 +607,11 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
     CUtensorMap tw, tx;
     cudaError_t e = make_tmap_2d_u8(&tw, g.w, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.ldw, kBlockK, 128);
     if (e != cudaSuccess) return e;
-    e = make_tmap_2d_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, BR);
+    if (g.win_rows > 0)
+        e = make_tmap_3d_windows_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.win_rows, (uint64_t)(g.M / g.win_rows),
+                                    (uint64_t)g.ldx, (uint64_t)g.win_stride, kBlockK, BR);
+    else
+        e = make_tmap_2d_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, BR);
     if (e != cudaSuccess) return e;
     static bool attr_set = false;
     if (!attr_set) {
@@ -593,9 +619,12 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
-    const long tiles = (long)((g.N + 127) / 128) * ((g.M + BR - 1) / BR);
+    const long row_tiles = g.win_rows > 0 ? (long)(g.M / g.win_rows) * ((g.win_rows + BR - 1) / BR)
+                                          : (long)((g.M + BR - 1) / BR);
+    const long tiles = (long)((g.N + 127) / 128) * row_tiles;
     const int grid = tiles < num_sms() ? (int)tiles : num_sms();
-    return launch_pdl(gemm_cm_kernel<BR, MODE, GK>, grid, kCmThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K, p);
+    return launch_pdl(gemm_cm_kernel<BR, MODE, GK>, grid, kCmThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K,
+                      g.win_rows, p);
 }
 
 template <int MODE, int GK>

@@ -99,6 +99,12 @@ struct GemmShape {
     const int8_t *w;
     int64_t ldw;  // row stride of W in bytes (multiple of 16)
     int M, N, K;
+    // optional (channel-major kernel): X as M / win_rows windows of win_rows
+    // rows, window w at x + w * win_stride; ldx may be smaller than K
+    // (overlapping rows: the im2col matrix of a convolution over a
+    // channels-last activation, read in place)
+    int win_rows = 0;
+    int64_t win_stride = 0;
 };
 
 // Launches the tcgen05 GEMM with the given epilogue on `stream`.

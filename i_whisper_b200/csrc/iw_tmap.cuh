@@ -47,4 +47,24 @@ inline cudaError_t make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// 3-D uint8 tensor: `count` windows of `rows` rows of `cols` bytes; row r of
+// window w starts at base + w*win_stride + r*ld. The row stride may be
+// smaller than a row (overlapping rows). Box [1, box_rows, box_cols], 128-byte
+// swizzle; out-of-bounds elements read as zero.
+inline cudaError_t make_tmap_3d_windows_u8(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                                           uint64_t count, uint64_t ld, uint64_t win_stride, uint32_t box_cols,
+                                           uint32_t box_rows) {
+    PFN_iwEncodeTiled fn = encode_tiled_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld & 15) || (win_stride & 15)) return cudaErrorMisalignedAddress;
+    cuuint64_t dims[3] = {cols, rows, count};
+    cuuint64_t strides[2] = {ld, win_stride};
+    cuuint32_t box[3] = {box_cols, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace iw

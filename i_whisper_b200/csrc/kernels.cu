@@ -480,6 +480,37 @@ cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K,
     return launch_pdl(im2col_kernel, (unsigned)blocks, 256, 0, st, x, out, B, Cin, Tin, K, stride, pad, Tout, ldo, channels_last);
 }
 
+// Channel-first [B][C][T] -> channels-last [B][T + front + back][C] with
+// `front` zero rows before and `back` after each window (the input of a
+// convolution run as a windowed GEMM). A 32x32 tile per block through
+// shared memory: coalesced reads along T, coalesced writes along C.
+__global__ void channels_last_pad_kernel(const int8_t *__restrict__ x, int B, int C, int T, int front, int back,
+                                         int8_t *__restrict__ out) {
+    pdl_wait();
+    pdl_launch();
+    __shared__ int8_t tile[32][33];
+    const int b = blockIdx.z;
+    const int Tp = T + front + back;
+    const int u0 = blockIdx.x * 32, c0 = blockIdx.y * 32;  // padded-row and channel origin
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+    for (int i = ty; i < 32; i += 8) {
+        const int c = c0 + i, t = u0 + tx - front;
+        tile[i][tx] = (c < C && t >= 0 && t < T) ? x[((int64_t)b * C + c) * T + t] : (int8_t)0;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int u = u0 + i, c = c0 + tx;
+        if (u < Tp && c < C) out[((int64_t)b * Tp + u) * C + c] = tile[tx][i];
+    }
+}
+
+cudaError_t channels_last_pad(const int8_t *x, int B, int C, int T, int front, int back, int8_t *out,
+                              cudaStream_t st) {
+    if (B <= 0 || C <= 0 || T <= 0) return cudaSuccess;
+    dim3 grid((T + front + back + 31) / 32, (C + 31) / 32, B);
+    return launch_pdl(channels_last_pad_kernel, grid, 256, 0, st, x, B, C, T, front, back, out);
+}
+
 // 2-D copy into a zero-padded buffer (row stride ldo >= cols).
 __global__ void pad_rows_kernel(const int8_t *__restrict__ x, int64_t rows, int64_t cols, int8_t *__restrict__ out,
                                 int64_t ldo) {

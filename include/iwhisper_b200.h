@@ -261,6 +261,15 @@ typedef struct iw_gemm_desc {
      * aligned); lets the kernel fetch each 128-channel tile's table with one
      * bulk copy. gelu_table must still be given. */
     const int8_t *gelu_table_tiled;
+    /* optional implicit-convolution operand: when x_window_rows > 0, X is
+     * M / x_window_rows windows of x_window_rows rows; row r of window w
+     * starts at x + w*x_window_stride + r*ldx (bytes; both multiples of 16).
+     * ldx may be smaller than K, so K-wide rows overlap: a k-tap, stride-s
+     * convolution over a zero-padded channels-last activation [W][rows'][C]
+     * is this GEMM with ldx = s*C, K = k*C and weights ordered (tap, channel).
+     * Needs the channel-major kernel (IW_EINVAL otherwise). */
+    int64_t x_window_rows;
+    int64_t x_window_stride;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */
@@ -328,6 +337,16 @@ int iw_layernorm32_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const
 int iw_layernorm64_ex(const int16_t *x, int64_t ldx, const int8_t *weight, const int32_t *bias,
                       uint8_t ln_multiplier, int8_t ln_shift, uint32_t out_multiplier, int8_t out_shift, int8_t *y,
                       int64_t ldy, int64_t rows, int64_t d, int32_t *rowsum_out, int32_t *rowsum_zero, void *stream);
+
+/* Channel-first x [B][C][T] -> channels-last out [B][T+front+back][C] with
+ * `front` zero rows before and `back` zero rows after each batch element:
+ * the padded input of a convolution run as a windowed GEMM
+ * (iw_gemm_desc.x_window_rows). B <= 65535. */
+int iw_channels_last_pad(const int8_t *x, int64_t B, int64_t C, int64_t T, int64_t front, int64_t back, int8_t *out,
+                         void *stream);
+/* Zero `count` rows of `bytes` bytes, `pitch` bytes apart (the padding rows
+ * of a windowed GEMM operand). */
+int iw_zero_rows(void *p, int64_t count, int64_t bytes, int64_t pitch, void *stream);
 
 /* im2col of the conv stem: row (b,t), column cin*K+k = x[b,cin,t*stride-pad+k]
  * (channels_last: x[b,t',cin]), zero outside; out row stride ldo >= Cin*K. */

@@ -274,6 +274,54 @@ def test_conv1d(ops, L, B, Cin, Tin, Cout, stride):
         assert np.array_equal(host(got), ref)
 
 
+@pytest.mark.parametrize("B,Cin,Tin,Cout,stride", [(2, 80, 3000, 384, 1), (3, 128, 40, 256, 1), (2, 384, 3000, 384, 2),
+                                                    (1, 256, 34, 128, 2)])
+def test_conv_windowed_gemm(L, B, Cin, Tin, Cout, stride):
+    """The conv stem as the model runs it: channels-last zero-padded input
+    read in place by the GEMM (x_window_rows, overlapping rows), weights in
+    (tap, channel) order; checked against the reference conv1d restatement
+    (all output rows, including the padding row the model zeroes)."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(Cin + Tin + stride)
+    x = rng.integers(-127, 128, (B, Cin, Tin), dtype=np.int8)
+    w = rng.integers(-127, 128, (Cout, Cin * 3), dtype=np.int8)
+    b = rng.integers(-5000, 5000, Cout, dtype=np.int32)
+    m, s_ = 2 ** 30 + 5, 6
+    ref = L.conv1d(x, w, b, m, s_, stride, 1)  # [B, Cout, Tout]
+    Tout = ref.shape[2]
+    st = torch.cuda.current_stream().cuda_stream
+    wt = dev(np.ascontiguousarray(w.reshape(Cout, Cin, 3).transpose(0, 2, 1).reshape(Cout, 3 * Cin)))
+    bias = dev(b)
+    if stride == 1:
+        # rows t' = t + 1 of a window read padded rows t'..t'+2: 2 zero rows in front, 1 behind
+        xcl = torch.empty(B * (Tin + 3), Cin, dtype=torch.int8, device="cuda")
+        _lib.call("iw_channels_last_pad", dev(x).data_ptr(), B, Cin, Tin, 2, 1, xcl.data_ptr(), st)
+        rows, stride_b, ldx, first = Tin + 1, (Tin + 3) * Cin, Cin, 1
+    else:
+        # output t reads rows 2t..2t+2 of a window with one zero row in front
+        xcl = torch.empty(B * (Tin + 1), Cin, dtype=torch.int8, device="cuda")
+        _lib.call("iw_channels_last_pad", dev(x).data_ptr(), B, Cin, Tin, 1, 0, xcl.data_ptr(), st)
+        rows, stride_b, ldx, first = Tout, (Tin + 1) * Cin, 2 * Cin, 0
+    y = torch.full((B * rows, Cout), 99, dtype=torch.int8, device="cuda")
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = xcl.data_ptr(), ldx, wt.data_ptr(), 3 * Cin, B * rows, Cout, 3 * Cin
+    d.mode, d.out, d.ldo, d.bias = _lib.IW_GEMM_INT8, y.data_ptr(), Cout, bias.data_ptr()
+    d.scalar_multiplier, d.scalar_shift = m, s_
+    d.x_window_rows, d.x_window_stride = rows, stride_b
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
+    got = host(y).reshape(B, rows, Cout)[:, first:first + Tout].transpose(0, 2, 1)
+    assert np.array_equal(got, ref)
+    # the zero-row helper clears the padding row of every window
+    if stride == 1:
+        _lib.call("iw_zero_rows", y.data_ptr(), B, Cout, rows * Cout, st)
+        assert not host(y).reshape(B, rows, Cout)[:, 0].any()
+    # a row count that does not divide M is rejected
+    d.x_window_rows = rows + 1
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
+
+
 @pytest.mark.parametrize("nm,ns", [(1, 1), (64, 64), (1, 64)])
 def test_add_requant15(ops, L, nm, ns):
     rng = np.random.default_rng(nm + ns)
