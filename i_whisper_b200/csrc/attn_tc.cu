@@ -324,6 +324,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t col = (uint32_t)(slice * SC);
         const RrsK k_rsq = rrs_k(p.rsqrt_offset), k_av = rrs_k(p.av_shift);  // output normalisation shifts
+        const bool epi_simple = k_rsq.sgn == -1 && k_av.sgn == -1;  // both shifts in [1, 31]
         int sb = 0, pb = 0, ob = 0;
         uint32_t sph = 0, pph = 0, oph = 0;
         // wait helper: every lane waits (the warp stays converged, which
@@ -487,14 +488,27 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     if (q < T) {
                         const int32_t inv = fisr(rsum, p.rsqrt_offset);
                         uint32_t w4[OC / 4];
+                        if (epi_simple) {
+                            // both shifts in [1, 31]: three-op rounding shifts
 #pragma unroll
-                        for (int u = 0; u < OC; ++u) {
-                            int32_t v = rrs_apply(wmul((int32_t)acc[u], inv), k_rsq);
-                            v = rrs_apply(wmul(v, inv), k_rsq);
-                            v = rrs_apply(wmul(v, (int32_t)p.av_mult), k_av);
-                            v = clampi(v, -127, 127);
-                            if ((u & 3) == 0) w4[u >> 2] = 0;
-                            w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                            for (int u = 0; u < OC; ++u) {
+                                int32_t v = wmul((int32_t)acc[u], inv);
+                                v = wmul(wadd(wadd(v, k_rsq.rnd), v >> 31) >> k_rsq.sh, inv);
+                                v = wmul(wadd(wadd(v, k_rsq.rnd), v >> 31) >> k_rsq.sh, (int32_t)p.av_mult);
+                                v = clampi(wadd(wadd(v, k_av.rnd), v >> 31) >> k_av.sh, -127, 127);
+                                if ((u & 3) == 0) w4[u >> 2] = 0;
+                                w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                            }
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < OC; ++u) {
+                                int32_t v = rrs_apply(wmul((int32_t)acc[u], inv), k_rsq);
+                                v = rrs_apply(wmul(v, inv), k_rsq);
+                                v = rrs_apply(wmul(v, (int32_t)p.av_mult), k_av);
+                                v = clampi(v, -127, 127);
+                                if ((u & 3) == 0) w4[u >> 2] = 0;
+                                w4[u >> 2] |= (uint32_t)(uint8_t)v << (8 * (u & 3));
+                            }
                         }
                         int8_t *o = p.out + (int64_t)(row0 + q) * p.ldo + h * 64 + slice * OC;
 #pragma unroll
