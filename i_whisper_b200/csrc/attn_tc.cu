@@ -68,8 +68,8 @@ constexpr int OFF_Q = 0;                          // two Q buffers
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
 constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
-constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // 2 x [SLICES][BQ] int32 cross-warp row max / sum
-constexpr int OFF_BAR = OFF_RED + 2 * SLICES * BQ * 4;
+constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // 3 x [SLICES][BQ] int32 cross-warp row max / sum / output sum
+constexpr int OFF_BAR = OFF_RED + 3 * SLICES * BQ * 4;
 constexpr int SMEM = 1024 + OFF_BAR + 512;
 constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
 constexpr uint32_t TMEM_O = 384;
@@ -87,6 +87,7 @@ struct AttnTcParams {
     uint32_t av_shift;    // clamp(av_s, 0, 32)
     uint32_t rsqrt_offset;
     int vt_ld;            // row stride (keys) of V^T
+    int32_t *rowsum_out;  // optional: += each output row's sum (the out-projection's zero-point term)
 };
 
 // K-major operand with 64-byte rows, 64-byte swizzle (8-row atoms of 512 B).
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                 }
             }
         };
-        int32_t *sRedMax = sRed, *sRedSum = sRed + SLICES * BQ;
+        int32_t *sRedMax = sRed, *sRedSum = sRed + SLICES * BQ, *sRedRow = sRed + 2 * SLICES * BQ;
         // Phase ph: pass 2 of this CTA's item ph-1 block by block interleaved
         // with pass 1 of its item ph, so that the light pass-1 blocks (a row
         // max) fill the Q.K^T round trip that the heavy pass-2 blocks hide.
@@ -515,9 +516,28 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         for (int c4 = 0; c4 < OC / 16; ++c4)
                             *reinterpret_cast<uint4 *>(o + 16 * c4) =
                                 make_uint4(w4[4 * c4], w4[4 * c4 + 1], w4[4 * c4 + 2], w4[4 * c4 + 3]);
+                        if (p.rowsum_out) {
+                            // this slice's share of the output row's sum (signed
+                            // bytes, four per dp4a), combined across slices below
+                            int32_t sum = 0;
+#pragma unroll
+                            for (int w = 0; w < OC / 4; ++w) sum = __dp4a((int32_t)w4[w], 0x01010101, sum);
+                            sRedRow[slice * BQ + r] = sum;
+                        }
                     }
                 }
                 if (++ob == 2) { ob = 0; oph ^= 1; }
+                if (p.rowsum_out) {
+                    // one atomic per row and head: slice-0 warps add the slices' sums
+                    bar_soft();
+                    const int q = q0 + r;
+                    if (slice == 0 && q < T) {
+                        int32_t sum = 0;
+#pragma unroll
+                        for (int sl = 0; sl < SLICES; ++sl) sum += sRedRow[sl * BQ + r];
+                        atomicAdd(p.rowsum_out + row0 + q, sum);
+                    }
+                }
             }
             if (has1) {
                 // combine the column slices of each row
@@ -642,6 +662,7 @@ cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, in
     p.av_shift = (uint32_t)clampi(a.av_shift, 0, 32);
     p.rsqrt_offset = a.rsqrt_offset;
     p.vt_ld = vt_ld;
+    p.rowsum_out = a.rowsum_out;
     static bool attr = false;
     if (!attr) {
         e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);

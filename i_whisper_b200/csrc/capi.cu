@@ -528,7 +528,6 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream) {
                     d->y_bs == d->Tq * d->ldy && (d->ldy % 16) == 0 && (reinterpret_cast<uintptr_t>(d->y) & 15) == 0 &&
                     d->vt_ld >= d->Tk && (d->vt_ld % 16) == 0 && (reinterpret_cast<uintptr_t>(d->vt) & 15) == 0;
     a.rowsum_out = d->row_sum_out;
-    if (tc && d->row_sum_out) return fail(IW_EINVAL, "iw_attention_ex: row_sum_out needs the CUDA-core path");
     if (tc)
         return cuda_check(iw::attention_tc(a, (int)d->B, (int)d->H, d->exp_table, d->vt, (int)d->vt_ld,
                                            d->vt_ready != 0, S(stream)),

@@ -311,9 +311,9 @@ typedef struct iw_attn_desc {
     /* 1: vt already holds V^T (written by the projection GEMM's vt_out), so
      * the call does not transpose V */
     int vt_ready;
-    /* optional (CUDA-core path): the sum of each int8 output row (b, q) is
-     * ADDED to row_sum_out[b*Tq + q] (zero it first) -- the zero-point row
-     * sums the output projection needs */
+    /* optional: the sum of each int8 output row (b, q) is ADDED to
+     * row_sum_out[b*Tq + q] (zero it first) -- the zero-point row sums the
+     * output projection needs */
     int32_t *row_sum_out;
 } iw_attn_desc;
 

@@ -541,8 +541,11 @@ def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
     a.qk_multiplier, a.qk_shift, a.frac_bits = 90, qk_s, fb
     a.av_multiplier, a.av_shift, a.rsqrt_offset = 200, 8, 16
     a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
+    rsum = torch.full((B * T,), 7, dtype=torch.int32, device="cuda")  # added to, not overwritten
+    a.row_sum_out = rsum.data_ptr()
     _lib.check(_lib.LIB.iw_attention_ex(ctypes.byref(a), st))
     assert np.array_equal(host(out).reshape(B, T, d), ref)
+    assert np.array_equal(host(rsum), ref.reshape(B * T, d).astype(np.int32).sum(1) + 7)
     assert _lib.device_status(clear=True) == 0
 
 
