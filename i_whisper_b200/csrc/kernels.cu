@@ -114,17 +114,28 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const int16_t *__restric
         // non-negative and the rounding shift by the even renorm shift rs
         // (<= 16) needs no sign term; a row with a wrapped (negative) square
         // takes the signed form.
-        int32_t mx = 0, mn = 0;
+        // |x - mean| <= 65535, so every square is exact as uint32: their
+        // unsigned max is the row's max square, and a row has a wrapped
+        // (negative int32) square exactly when that max is >= 2^31
+        uint32_t mxu = 0;
         int32_t sq[G * 4];
 #pragma unroll
         for (int i = 0; i < G * 4; ++i) {
             v[i] -= mean;
             sq[i] = wmul(v[i], v[i]);
-            mx = max(mx, sq[i]);
-            mn = min(mn, sq[i]);
+            mxu = max(mxu, (uint32_t)sq[i]);
         }
-        mx = warp_max(mx);
-        const bool wrapped = __any_sync(0xffffffffu, mn < 0);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mxu = max(mxu, __shfl_xor_sync(0xffffffffu, mxu, o));
+        const bool wrapped = (mxu >> 31) != 0;
+        int32_t mx = (int32_t)mxu;
+        if (wrapped) {
+            // the reference's max over the int32 (wrapped) squares
+            mx = 0;
+#pragma unroll
+            for (int i = 0; i < G * 4; ++i) mx = max(mx, sq[i]);
+            mx = warp_max(mx);
+        }
         int32_t rs = bit_length_nonneg(mx) - 16;
         rs = rs < 0 ? 0 : rs;
         rs = (rs + 1) & ~1;
