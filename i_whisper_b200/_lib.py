@@ -55,6 +55,8 @@ SIGNATURES = {
     "iw_im2col": [_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P],
     "iw_channels_last_pad": [_P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "iw_zero_rows": [_P, _I64, _I64, _I64, _P],
+    "iw_set_wait_timeout_ns": [C.c_uint64],
+    "iw_selftest_wait_timeout": [_P, _P],
     "iw_embed_add_requant15_dev": [_P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "iw_kv_append": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "iw_greedy_step": [_P, _I64, _P],

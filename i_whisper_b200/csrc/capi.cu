@@ -103,6 +103,17 @@ const char *iw_last_error(void) { return g_err.c_str(); }
 
 int iw_abi_version(void) { return 1; }
 
+int iw_set_wait_timeout_ns(uint64_t ns) {
+    if (ns == 0) return fail(IW_EINVAL, "iw_set_wait_timeout_ns: the bound must be positive");
+    const unsigned long long v = ns;
+    return cuda_check(cudaMemcpyToSymbol(iw::g_wait_timeout_ns, &v, sizeof(v)), "iw_set_wait_timeout_ns");
+}
+
+int iw_selftest_wait_timeout(int32_t *gave_up, void *stream) {
+    if (!gave_up) return fail(IW_EINVAL, "iw_selftest_wait_timeout: null result pointer");
+    return cuda_check(iw::selftest_wait(gave_up, S(stream)), "iw_selftest_wait_timeout");
+}
+
 int iw_device_status(uint32_t *status, int clear) {
     if (int r = cuda_check(cudaDeviceSynchronize(), "iw_device_status")) return r;
     uint32_t v = 0;

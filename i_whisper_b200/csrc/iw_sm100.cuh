@@ -20,6 +20,10 @@
 
 namespace iw {
 
+// The bound of every mbarrier wait (ns), IW_WAIT_TIMEOUT_NS unless
+// iw_set_wait_timeout_ns changed it (the failure-path self-test shortens it).
+__device__ unsigned long long g_wait_timeout_ns = IW_WAIT_TIMEOUT_NS;
+
 IW_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // The dynamic shared array rounded up to a 1024-byte boundary (swizzled
@@ -78,7 +82,7 @@ IW_DEV bool mbar_wait(uint64_t *bar, uint32_t parity) {
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait_suspend(bar, parity, 200000u)) return true;
-        if ((it & 255u) == 0 && globaltimer_ns() - t0 > IW_WAIT_TIMEOUT_NS) {
+        if ((it & 255u) == 0 && globaltimer_ns() - t0 > g_wait_timeout_ns) {
             atomicOr(&g_device_status, IW_DEVERR_WAIT_TIMEOUT);
             return false;
         }

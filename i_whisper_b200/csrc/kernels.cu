@@ -491,6 +491,24 @@ cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K,
     return launch_pdl(im2col_kernel, (unsigned)blocks, 256, 0, st, x, out, B, Cin, Tin, K, stride, pad, Tout, ldo, channels_last);
 }
 
+// Failure-path self-test: one thread waits, through the same bounded
+// mbar_wait every tcgen05 kernel uses, on a barrier nothing arrives on. The
+// wait gives up after the current bound, records IW_DEVERR_WAIT_TIMEOUT in
+// the device status word and the kernel returns: no fault, no hang.
+__global__ void selftest_wait_kernel(int *gave_up) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        *gave_up = mbar_wait(&bar, 0) ? 0 : 1;
+    }
+}
+
+cudaError_t selftest_wait(int *gave_up, cudaStream_t st) {
+    selftest_wait_kernel<<<1, 32, 0, st>>>(gave_up);
+    return cudaGetLastError();
+}
+
 // Channel-first [B][C][T] -> channels-last [B][T + front + back][C] with
 // `front` zero rows before and `back` after each window (the input of a
 // convolution run as a windowed GEMM). A 32x32 tile per block through

@@ -66,6 +66,8 @@ cudaError_t residual15(const int32_t *br, const int16_t *r, uint16_t m, int16_t 
 cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *addend, const uint16_t *mult,
                           const int8_t *shift, int16_t *y, int B, int T, int C, int n_mult, int n_shift, int offset,
                           const int32_t *offset_dev, cudaStream_t st);
+// Bounded-wait self-test (see kernels.cu); *gave_up = 1 when the wait expired.
+cudaError_t selftest_wait(int *gave_up, cudaStream_t st);
 cudaError_t channels_last_pad(const int8_t *x, int B, int C, int T, int front, int back, int8_t *out,
                               cudaStream_t st);
 cudaError_t im2col(const int8_t *x, int8_t *out, int B, int Cin, int Tin, int K, int stride, int pad, int Tout,

@@ -46,6 +46,13 @@ int iw_abi_version(void);
  * (bit 0: a bounded in-kernel wait timed out; bit 1: a LayerNorm64
  * variance did not fit INT32 in iw_layernorm64_ex) and clears it if `clear`. */
 int iw_device_status(uint32_t *status, int clear);
+/* Bound (ns) of every in-kernel mbarrier wait; default 2 s. */
+int iw_set_wait_timeout_ns(uint64_t ns);
+/* Failure-path self-test: a one-thread kernel waits, through the same
+ * bounded wait the tcgen05 kernels use, on a barrier nothing completes;
+ * when the bound expires it sets bit 0 of the device status word, writes
+ * 1 to *gave_up (device int32) and returns. Nothing faults or hangs. */
+int iw_selftest_wait_timeout(int32_t *gave_up, void *stream);
 
 /* linear8_{scalar,simd} -- linear8_scalar.cpp:30-84; pybind.cpp:51-70.
  * x [M,K] int8, weight [N,K] int8, bias [N] int32?, weight_zero [N] int8?,

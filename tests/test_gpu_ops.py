@@ -372,6 +372,28 @@ def test_error_paths(ops):
                              torch.zeros(100, dtype=torch.int8, device="cuda"), None, 1, 0, 1, 0)
 
 
+def test_bounded_wait_expires_cleanly():
+    """Failure detection on the device without a fault: with the wait bound
+    shortened, a wait on a barrier nothing completes gives up, the status word
+    records it, and the context stays usable for the next kernels."""
+    from i_whisper_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("iw_set_wait_timeout_ns", 2_000_000)  # 2 ms
+    try:
+        _lib.call("iw_selftest_wait_timeout", flag.data_ptr(), st)
+        status = _lib.device_status(clear=True)
+    finally:
+        _lib.call("iw_set_wait_timeout_ns", 2_000_000_000)
+    assert status & 1
+    assert int(flag.item()) == 1
+    x = torch.arange(64, dtype=torch.int32, device="cuda")
+    assert int((x * 2).sum().item()) == 4032  # the context still works
+    assert _lib.device_status(clear=True) == 0
+
+
 def test_device_status_clean():
     from i_whisper_b200 import _lib
     torch.cuda.synchronize()
