@@ -175,7 +175,8 @@ def save_int_checkpoint(dims: ModelDims, sd: Dict[str, np.ndarray], prefix: str,
     from safetensors.numpy import save_file
     d = os.path.join(prefix, f"iwhisper-{model_name}")
     os.makedirs(d, exist_ok=True)
-    save_file({k: np.ascontiguousarray(v) for k, v in sd.items()}, os.path.join(d, "model.safetensors"),
+    # np.require keeps 0-d tensors (qk_frac_bits) 0-d; ascontiguousarray would make them [1]
+    save_file({k: np.require(v, requirements="C") for k, v in sd.items()}, os.path.join(d, "model.safetensors"),
               metadata={"format": FORMAT, "format_version": str(FORMAT_VERSION)})
     with open(os.path.join(d, "config.json"), "w", encoding="utf-8") as f:
         json.dump({"format": FORMAT, "format_version": FORMAT_VERSION, "model_name": model_name,
