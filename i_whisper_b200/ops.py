@@ -323,6 +323,75 @@ def pv_norm_requant_cuda(p, v, row_sum, av_multiplier, av_shift, rsqrt_offset: i
     return y
 
 
+def _accum_i32(x2d, w2d, y2d):
+    """y2d [M,N] int32 = x2d [M,K] @ w2d [N,K]^T with wrapping int32 sums,
+    through the tensor-core accumulator GEMM (iw_linear8_accum). Views must be
+    contiguous; K == 0 gives zeros, as the reference's empty sums do."""
+    M, K = x2d.shape
+    N = w2d.shape[0]
+    if M == 0 or N == 0:
+        return
+    if K == 0:
+        y2d.zero_()
+        return
+    _lib.call("iw_linear8_accum", x2d.data_ptr(), w2d.data_ptr(), None, None, y2d.data_ptr(), M, K, N, _stream())
+
+
+def qk_cuda(q, k):
+    """``_C.qk_simd`` (attention_torch.cpp:10-114, qk_scalar attention_scalar.cpp:130):
+    q [B,H,Tq,D] int8, k [B,H,Tk,D] int8 -> int32 [B,H,Tq,Tk], the raw
+    Q·Kᵀ sums. One accumulator GEMM per (batch, head)."""
+    _chk(q, "q", "int8"); _chk(k, "k", "int8")
+    if q.dim() != 4:
+        raise RuntimeError("q must be [B,H,Tq,D]")
+    if k.dim() != 4:
+        raise RuntimeError("k must be [B,H,Tk,D]")
+    if q.shape[0] != k.shape[0]:
+        raise RuntimeError("batch mismatch")
+    if q.shape[1] != k.shape[1]:
+        raise RuntimeError("head count mismatch")
+    if q.shape[3] != k.shape[3]:
+        raise RuntimeError("head dimension mismatch")
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    y = torch.empty(B, H, Tq, Tk, dtype=torch.int32, device=q.device)
+    qf, kf, yf = q.reshape(B * H, Tq, D), k.reshape(B * H, Tk, D), y.view(B * H, Tq, Tk)
+    for i in range(B * H):
+        _accum_i32(qf[i], kf[i], yf[i])
+    return y
+
+
+def pv_cuda(p, v):
+    """``_C.pv_simd`` (attention_torch.cpp:401-521, pv_scalar attention_scalar.cpp:590):
+    p [B,H,Tq,Tk] uint8, v [B,H,D,Tk] int8 (V transposed) -> int32
+    [B,H,Tq,D], the raw P·V sums. The int8 GEMM takes signed operands, so
+    p = lo + 128·hi with lo = p & 127 and hi = p >> 7 (both within int8), and
+    the sum is Σ lo·v + 128·Σ hi·v; int32 wrapping sums make the split exact."""
+    _chk(p, "p", "uint8"); _chk(v, "v", "int8")
+    if p.dim() != 4:
+        raise RuntimeError("p must be [B,H,Tq,Tk]")
+    if v.dim() != 4:
+        raise RuntimeError("v must be [B,H,D,Tk]")
+    if p.shape[0] != v.shape[0]:
+        raise RuntimeError("batch mismatch")
+    if p.shape[1] != v.shape[1]:
+        raise RuntimeError("head count mismatch")
+    if p.shape[3] != v.shape[3]:
+        raise RuntimeError("key length mismatch")
+    B, H, Tq, Tk = p.shape
+    D = v.shape[2]
+    y = torch.empty(B, H, Tq, D, dtype=torch.int32, device=p.device)
+    lo = torch.bitwise_and(p, 127).view(torch.int8).reshape(B * H, Tq, Tk)
+    hi = torch.bitwise_right_shift(p, 7).view(torch.int8).reshape(B * H, Tq, Tk)
+    vf, yf = v.reshape(B * H, D, Tk), y.view(B * H, Tq, D)
+    y_hi = torch.empty(Tq, D, dtype=torch.int32, device=p.device)
+    for i in range(B * H):
+        _accum_i32(lo[i], vf[i], yf[i])
+        _accum_i32(hi[i], vf[i], y_hi)
+        yf[i].add_(y_hi, alpha=128)
+    return y
+
+
 def attention_cuda(q, k, v, n_head: int, qk_multiplier, qk_shift, frac_bits, av_multiplier, av_shift,
                    rsqrt_offset: int = 16, mask_mode: int = 0, mask=None, out=None):
     """Fused A1-A3 (MultiHeadAttention_int.qkv_attention, model_int.py:774-1042)
@@ -342,8 +411,8 @@ def attention_cuda(q, k, v, n_head: int, qk_multiplier, qk_shift, frac_bits, av_
 # ---------------------------------------------------------------------------
 # Conv1d (conv1d_torch.cpp:136-360), Add+Requant15, classifier
 # ---------------------------------------------------------------------------
-def conv1d_cuda(input, weight, bias, multiplier, shift, stride: int, padding: int):
-    """``_C.conv1d_simd`` (conv1d_scalar.cpp:186-288)."""
+def _conv1d_shape(input, weight, bias, stride, padding):
+    """check_conv1d_common (conv1d_torch.cpp:26-133) -> (B, Cin, Tin, Cout, K, Tout)."""
     _chk(input, "input", "int8"); _chk(weight, "weight", "int8")
     if input.dim() != 3:
         raise RuntimeError("input must be [B,Cin,Tin]")
@@ -357,13 +426,30 @@ def conv1d_cuda(input, weight, bias, multiplier, shift, stride: int, padding: in
     Cout = weight.shape[0]
     if Cin <= 0:
         raise RuntimeError("input channel count must be positive")
+    if Tin <= 0:
+        raise RuntimeError("input length must be positive")
+    if Cout <= 0:
+        raise RuntimeError("output channel count must be positive")
     if weight.shape[1] % Cin != 0:
         raise RuntimeError("weight.size(1) must be divisible by input channels")
     K = weight.shape[1] // Cin
+    if K <= 0:
+        raise RuntimeError("kernel size must be positive")
+    num = Tin + 2 * padding - K
+    if num < 0:
+        raise RuntimeError("invalid Conv1d geometry: output length would be non-positive")
     if bias is not None:
         _chk(bias, "bias", "int32")
-        if bias.dim() != 1 or bias.numel() != Cout:
+        if bias.dim() != 1:
+            raise RuntimeError("bias must be [Cout]")
+        if bias.numel() != Cout:
             raise RuntimeError("bias.numel() must equal output channels")
+    return B, Cin, Tin, Cout, K, num // stride + 1
+
+
+def conv1d_cuda(input, weight, bias, multiplier, shift, stride: int, padding: int):
+    """``_C.conv1d_simd`` (conv1d_scalar.cpp:186-288)."""
+    B, Cin, Tin, Cout, K, Tout = _conv1d_shape(input, weight, bias, stride, padding)
     # scalar parameters are read on the host; they may live on either device
     if isinstance(multiplier, torch.Tensor):
         if multiplier.dtype != torch.uint32:
@@ -375,13 +461,28 @@ def conv1d_cuda(input, weight, bias, multiplier, shift, stride: int, padding: in
             raise RuntimeError(f"shift must be int8, got {shift.dtype}")
         if shift.numel() != 1:
             raise RuntimeError("shift must contain exactly one element")
-    num = Tin + 2 * padding - K
-    if num < 0:
-        raise RuntimeError("invalid Conv1d geometry: output length would be non-positive")
-    Tout = num // stride + 1
     y = torch.empty(B, Cout, Tout, dtype=torch.int8, device=input.device)
     _lib.call("iw_conv1d", input.data_ptr(), weight.data_ptr(), _p(bias), _scalar(multiplier, "multiplier"),
               _scalar(shift, "shift"), stride, padding, y.data_ptr(), B, Cin, Tin, Cout, K, _stream())
+    return y
+
+
+def conv1d_accum_cuda(input, weight, bias, stride: int, padding: int):
+    """``_C.conv1d_accum_simd`` (conv1d_torch.cpp:136-209): the int32
+    accumulators [B,Cout,Tout] before requantisation, bias included. im2col
+    (column cin*K + k, the weight's flattened order) and one accumulator GEMM
+    with the bias in its epilogue."""
+    B, Cin, Tin, Cout, K, Tout = _conv1d_shape(input, weight, bias, stride, padding)
+    y = torch.empty(B, Cout, Tout, dtype=torch.int32, device=input.device)
+    if B == 0:
+        return y
+    cols = torch.empty(B * Tout, Cin * K, dtype=torch.int8, device=input.device)
+    _lib.call("iw_im2col", input.data_ptr(), cols.data_ptr(), B, Cin, Tin, K, stride, padding, Tout, Cin * K, 0,
+              _stream())
+    acc = torch.empty(B * Tout, Cout, dtype=torch.int32, device=input.device)
+    _lib.call("iw_linear8_accum", cols.data_ptr(), weight.data_ptr(), _p(bias), None, acc.data_ptr(), B * Tout,
+              Cin * K, Cout, _stream())
+    y.copy_(acc.view(B, Tout, Cout).permute(0, 2, 1))
     return y
 
 
@@ -418,8 +519,8 @@ def embed_add_requant15_cuda(table, tokens, pe, offset: int, multiplier, shift, 
     return y
 
 
-def classifier_cuda(input, weight, multiplier, shift):
-    """``_C.classifier_simd`` (classifier_scalar.cpp:91-140)."""
+def _classifier_shape(input, weight):
+    """check_classifier_common (classifier_torch.cpp:23-75) -> (B, T, K, N)."""
     _chk(input, "input", "int8"); _chk(weight, "weight", "int8")
     if input.dim() != 3:
         raise RuntimeError("input must be [B,T,K]")
@@ -431,7 +532,31 @@ def classifier_cuda(input, weight, multiplier, shift):
         raise RuntimeError("weight hidden size must match input")
     if K <= 0:
         raise RuntimeError("hidden size must be positive")
+    if N <= 0:
+        raise RuntimeError("vocabulary size must be positive")
+    return B, T, K, N
+
+
+def classifier_cuda(input, weight, multiplier, shift):
+    """``_C.classifier_simd`` (classifier_scalar.cpp:91-140)."""
+    B, T, K, N = _classifier_shape(input, weight)
     y = torch.empty(B, T, N, dtype=torch.int8, device=input.device)
     _lib.call("iw_classifier", input.data_ptr(), weight.data_ptr(), _scalar(multiplier, "multiplier"),
               _scalar(shift, "shift"), y.data_ptr(), B * T, K, N, _stream())
     return y
+
+
+def classifier_accum_cuda(input, weight):
+    """``_C.classifier_accum_simd`` (classifier_torch.cpp:78-143): the raw
+    int32 sums x·Eᵀ [B,T,V] before requantisation."""
+    B, T, K, N = _classifier_shape(input, weight)
+    y = torch.empty(B, T, N, dtype=torch.int32, device=input.device)
+    _accum_i32(input.view(B * T, K), weight, y.view(B * T, N))
+    return y
+
+
+def linear32_accum_cuda_debug(x, weight, bias=None, weight_zero=None):
+    """``_C.linear32_accum_simd_debug`` (linear32_scalar.cpp:9-63): the same
+    int32 accumulator as Linear8's (x·Wᵀ + bias − wz·Σx, wrapping), which the
+    Linear8 accumulator entry point computes."""
+    return linear8_accum_cuda_debug(x, weight, bias, weight_zero)

@@ -357,6 +357,31 @@ def test_classifier(ops, L, M, K, N):
         assert np.array_equal(host(got), ref)
 
 
+def test_accumulator_mirrors(ops, L):
+    """The accumulator-only operators (qk, pv, conv1d_accum, classifier_accum,
+    linear32_accum_debug) against the oracle, at tails and full ranges."""
+    rng = np.random.default_rng(77)
+    for B, H, Tq, Tk, D in [(2, 3, 5, 17, 64), (1, 16, 3, 1500, 64), (1, 2, 4, 9, 7)]:
+        q = rng.integers(-128, 128, (B, H, Tq, D), dtype=np.int8)
+        k = rng.integers(-128, 128, (B, H, Tk, D), dtype=np.int8)
+        assert np.array_equal(host(ops.qk_cuda(dev(q), dev(k))), L.qk(q, k))
+        p = rng.integers(0, 256, (B, H, Tq, Tk), dtype=np.uint8)
+        vt = rng.integers(-128, 128, (B, H, D, Tk), dtype=np.int8)
+        assert np.array_equal(host(ops.pv_cuda(dev(p), dev(vt))), L.pv(p, vt))
+    for B, Cin, Tin, Cout, stride in [(2, 80, 64, 48, 1), (1, 48, 61, 32, 2)]:
+        x = rng.integers(-128, 128, (B, Cin, Tin), dtype=np.int8)
+        w = rng.integers(-128, 128, (Cout, Cin * 3), dtype=np.int8)
+        b = rng.integers(-(2 ** 20), 2 ** 20, Cout, dtype=np.int32)
+        got = ops.conv1d_accum_cuda(dev(x), dev(w), dev(b), stride, 1)
+        assert np.array_equal(host(got), L.conv1d_accum(x, w, b, stride, 1))
+    x = rng.integers(-128, 128, (2, 3, 384), dtype=np.int8)
+    e = rng.integers(-128, 128, (51865, 384), dtype=np.int8)
+    assert np.array_equal(host(ops.classifier_accum_cuda(dev(x), dev(e))), L.classifier_accum(x, e))
+    x, w, b, wz, _, _ = rand_linear(rng, 33, 100, 70)
+    got = ops.linear32_accum_cuda_debug(dev(x), dev(w), dev(b), dev(wz))
+    assert np.array_equal(host(got), L.linear8_accum(x, w, b, wz))
+
+
 def test_error_paths(ops):
     x = torch.zeros(2, 16, dtype=torch.int8, device="cuda")
     w = torch.zeros(4, 16, dtype=torch.int8, device="cuda")
