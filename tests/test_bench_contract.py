@@ -1,0 +1,47 @@
+"""bench.py's reference arm and its JSON line, on the CPU.
+
+The reference arm times the reference's own scalar C++ kernels (or the
+oracle port where they were not built) on the host cores. This test runs it
+on the tiny model with one small sample step and checks the keys and units
+of the line it prints, and that a rank other than 0 prints nothing and
+exits 0, as a torchrun launch of both arms requires."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ARGS = [sys.executable, "bench.py", "--impl", "reference", "--model", "tiny", "--steps", "1", "--warmup", "0",
+        "--cpu-rows", "16"]
+
+
+def _run(extra_env=None):
+    env = dict(os.environ, **(extra_env or {}))
+    return subprocess.run(ARGS, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+
+
+def test_reference_arm_line():
+    r = _run()
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["value"] > 0 and d["unit"] == "windows/s" and d["higher_is_better"] is True
+    assert d["steps"] == 1 and d["warmup"] == 0 and d["n_gpus"] == 1
+    assert "whisper-tiny" in d["config"]["workload"]
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "windows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the timed sample step, not the extrapolated window time
+    assert d["ms_per_step"] <= 1e3 * d["wall_s"] + 100
+    assert d["ms_per_window_extrapolated"] > 0
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
