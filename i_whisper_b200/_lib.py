@@ -27,6 +27,8 @@ _U8, _I8, _U16, _U32, _I32 = C.c_uint8, C.c_int8, C.c_uint16, C.c_uint32, C.c_in
 SIGNATURES = {
     "iw_linear8": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "iw_linear8_accum": [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
+    "iw_linear8_requant": [_P, _P, _P, _P, _I64, _I64, _P],
+    "iw_rounding_rshift": [_P, C.c_uint32, _P, _I64, _P],
     "iw_linear32": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P],
     "iw_linear32_residual15": [_P, _P, _P, _P, _P, _P, _P, _U16, _P, _I64, _I64, _I64, _P],
     "iw_residual15": [_P, _P, _U16, _P, _I64, _P],

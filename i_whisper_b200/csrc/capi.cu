@@ -139,6 +139,19 @@ int iw_linear8_accum(const int8_t *x, const int8_t *weight, const int32_t *bias,
                       S(stream), "iw_linear8_accum");
 }
 
+int iw_linear8_requant(const int32_t *acc, const uint32_t *multiplier, const int8_t *shift, int32_t *y, int64_t M,
+                       int64_t N, void *stream) {
+    if (M < 0 || N <= 0) return fail(IW_EINVAL, "iw_linear8_requant: invalid shape M=%lld N=%lld", (long long)M,
+                                     (long long)N);
+    if (!multiplier || !shift) return fail(IW_EINVAL, "iw_linear8_requant: multiplier and shift are required");
+    return cuda_check(iw::requant_rows(acc, multiplier, shift, 0u, y, M * N, N, S(stream)), "iw_linear8_requant");
+}
+
+int iw_rounding_rshift(const int32_t *x, uint32_t shift, int32_t *y, int64_t numel, void *stream) {
+    if (numel < 0) return fail(IW_EINVAL, "iw_rounding_rshift: invalid numel");
+    return cuda_check(iw::requant_rows(x, nullptr, nullptr, shift, y, numel, 1, S(stream)), "iw_rounding_rshift");
+}
+
 int iw_linear32(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
                 const uint32_t *multiplier, const int8_t *shift, int32_t *y, int64_t M, int64_t K, int64_t N,
                 void *stream) {
@@ -182,7 +195,8 @@ __global__ void any_negative_kernel(const int32_t *x, int64_t n, int *flag) {
         if (x[i] < 0) atomicExch(flag, 1);
 }
 
-static int check_nonnegative(const int32_t *x, int64_t n, cudaStream_t st, const char *name, const char *msg) {
+static int check_nonnegative(const int32_t *x, int64_t n, cudaStream_t st, const char *name, const char *msg,
+                             int status = IW_EVALUE) {
     if (n <= 0) return IW_OK;
     Scratch f(st);
     if (int r = cuda_check(f.alloc(sizeof(int)), name)) return r;
@@ -193,12 +207,14 @@ static int check_nonnegative(const int32_t *x, int64_t n, cudaStream_t st, const
     int h = 0;
     if (int r = cuda_check(cudaMemcpyAsync(&h, f.p, sizeof(int), cudaMemcpyDeviceToHost, st), name)) return r;
     if (int r = cuda_check(cudaStreamSynchronize(st), name)) return r;
-    if (h) return fail(IW_EVALUE, "%s", msg);
+    if (h) return fail(status, "%s", msg);
     return IW_OK;
 }
 
 int iw_layernorm32_rsqrt(const int32_t *variance, int32_t *invstd, int64_t numel, void *stream) {
-    if (int r = check_nonnegative(variance, numel, S(stream), "iw_layernorm32_rsqrt", "input must be non-negative"))
+    // a TORCH_CHECK in the reference (layernorm_torch.cpp:120-122): RuntimeError, not ValueError
+    if (int r = check_nonnegative(variance, numel, S(stream), "iw_layernorm32_rsqrt", "input must be non-negative",
+                                  IW_EINVAL))
         return r;
     return cuda_check(iw::fisr_vec(variance, invstd, numel, 13u, S(stream)), "iw_layernorm32_rsqrt");
 }

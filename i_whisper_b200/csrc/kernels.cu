@@ -414,6 +414,34 @@ cudaError_t residual15(const int32_t *br, const int16_t *r, uint16_t m, int16_t 
 }
 
 // ---------------------------------------------------------------------------
+// Requantise-only debug paths (linear8_requant_scalar, linear8_scalar.cpp:130-150,
+// via fixedpoint::requant; rounding_rshift_debug, pybind.cpp:22-43):
+// with `mult` set, y[m,n] = rrs(mulh(x[m,n], mult[n]), (u32)shift[n]) with no
+// clamp; without it, y = rrs(x, shamt) elementwise (M*N elements).
+// ---------------------------------------------------------------------------
+__global__ void requant_rows_kernel(const int32_t *__restrict__ x, const uint32_t *__restrict__ mult,
+                                    const int8_t *__restrict__ shift, uint32_t shamt, int32_t *__restrict__ y,
+                                    int64_t n, int64_t N) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        if (mult) {
+            const int64_t c = i % N;
+            y[i] = rrs(mulh(x[i], mult[c]), (uint32_t)(int32_t)shift[c]);
+        } else {
+            y[i] = rrs(x[i], shamt);
+        }
+    }
+}
+
+cudaError_t requant_rows(const int32_t *x, const uint32_t *mult, const int8_t *shift, uint32_t shamt, int32_t *y,
+                         int64_t n, int64_t N, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    requant_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, mult, shift, shamt, y, n, N);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Add + requant to INT15 (add_requant15_scalar.cpp:29-80). With `tokens`
 // set, the int8 input row is gathered from the embedding table
 // (TextDecoder_int.forward, model_int.py:1411-1428) and the addend row is

@@ -63,6 +63,8 @@ cudaError_t layernorm32_stats(const int16_t *x, int rows, int d, int32_t *mean, 
 cudaError_t fisr_vec(const int32_t *x, int32_t *y, int64_t n, uint32_t off, cudaStream_t st);
 cudaError_t gelu(const int8_t *x, int8_t *y, int64_t n, int channels, const GeluParams &g, cudaStream_t st);
 cudaError_t residual15(const int32_t *br, const int16_t *r, uint16_t m, int16_t *y, int64_t n, cudaStream_t st);
+cudaError_t requant_rows(const int32_t *x, const uint32_t *mult, const int8_t *shift, uint32_t shamt, int32_t *y,
+                         int64_t n, int64_t N, cudaStream_t st);
 cudaError_t add_requant15(const int8_t *x, const int64_t *tokens, const int8_t *addend, const uint16_t *mult,
                           const int8_t *shift, int16_t *y, int B, int T, int C, int n_mult, int n_shift, int offset,
                           const int32_t *offset_dev, cudaStream_t st);

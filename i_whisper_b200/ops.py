@@ -106,6 +106,67 @@ def linear8_accum_cuda_debug(x, weight, bias=None, weight_zero=None):
     return y
 
 
+def _requant_checks(input, multiplier, shift):
+    """Argument checks of the requantise-only debug ops (linear8_torch.cpp:344-361,
+    linear32_torch.cpp:334-351) -> (M, N)."""
+    _chk(input, "input", "int32"); _chk(multiplier, "multiplier", "uint32"); _chk(shift, "shift", "int8")
+    if input.dim() < 1:
+        raise RuntimeError(f"input must have at least one dimension, got {input.dim()}")
+    if multiplier.dim() != 1:
+        raise RuntimeError(f"multiplier should be a 1D tensor, got {multiplier.dim()}")
+    if shift.dim() != 1:
+        raise RuntimeError(f"shift should be a 1D tensor, got {shift.dim()}")
+    N = input.shape[-1]
+    if N != multiplier.numel():
+        raise RuntimeError(f"input.size(-1) must equal multiplier's number of elements, got {N} "
+                           f"expected {multiplier.numel()}")
+    if multiplier.numel() != shift.numel():
+        raise RuntimeError(f"multiplier's number of elements must equal shift's number of elements, got "
+                           f"{multiplier.numel()} expected {shift.numel()}")
+    return (input.numel() // N if N else 0), N
+
+
+def linear8_requant_cuda_debug(input, multiplier, shift):
+    """``_C.linear8_requant_scalar_debug`` (linear8_torch.cpp:336-387): int32
+    accumulators -> rrs(mulh(acc, m[n]), (u32)s[n]) as int32, without the
+    final int8 clamp of Linear8."""
+    M, N = _requant_checks(input, multiplier, shift)
+    y = torch.empty(input.shape, dtype=torch.int32, device=input.device)
+    if M > 0:
+        _lib.call("iw_linear8_requant", input.data_ptr(), multiplier.data_ptr(), shift.data_ptr(), y.data_ptr(), M, N,
+                  _stream())
+    return y
+
+
+def linear32_requant_cuda_debug(input, multiplier, shift):
+    """``_C.linear32_requant_scalar_debug`` (linear32_torch.cpp:326-377): int32
+    accumulators -> (int32)((u32)mulh(acc, m[n]) << s[n]), 0 for s >= 32.
+    Each row m is the bias of a one-row Linear32 GEMM whose x and weight are
+    zero, so the GEMM's requantisation epilogue sees acc = input[m, n]
+    exactly; one launch per row (a debug path)."""
+    M, N = _requant_checks(input, multiplier, shift)
+    y = torch.empty(input.shape, dtype=torch.int32, device=input.device)
+    if M == 0:
+        return y
+    rows, out = input.view(M, N), y.view(M, N)
+    zx = torch.zeros(1, 16, dtype=torch.int8, device=input.device)
+    zw = torch.zeros(N, 16, dtype=torch.int8, device=input.device)
+    for m in range(M):
+        _lib.call("iw_linear32", zx.data_ptr(), zw.data_ptr(), rows[m].data_ptr(), None, multiplier.data_ptr(),
+                  shift.data_ptr(), out[m].data_ptr(), 1, 16, N, _stream())
+    return y
+
+
+def rounding_rshift_debug_cuda(x, shift):
+    """``_C.rounding_rshift_debug`` (pybind.cpp:22-43): fixedpoint
+    rounding_rshift of every int32 element by shift[0] (uint32)."""
+    _chk(x, "x", "int32"); _chk(shift, "shift", "uint32")
+    y = torch.empty_like(x)
+    _lib.call("iw_rounding_rshift", x.data_ptr(), _scalar(shift.reshape(-1)[:1], "shift"), y.data_ptr(), x.numel(),
+              _stream())
+    return y
+
+
 def linear32_cuda(x, weight, bias=None, weight_zero=None, multiplier=None, shift=None):
     """``_C.linear32_simd`` (linear32_scalar.cpp:96-129)."""
     M, K, N = _linear_checks(x, weight, bias, weight_zero, multiplier, shift)

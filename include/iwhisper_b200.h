@@ -66,6 +66,16 @@ int iw_linear8(const int8_t *x, const int8_t *weight, const int32_t *bias, const
 int iw_linear8_accum(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,
                      int32_t *y, int64_t M, int64_t K, int64_t N, void *stream);
 
+/* linear8_requant_scalar_debug -- linear8_scalar.cpp:130-150 (fixedpoint::requant,
+ * common/fixedpoint.h); pybind.cpp:74-76. acc [M,N] int32 ->
+ * y = rounding_rshift(mulh(acc, multiplier[n]), (uint32)shift[n]), int32, no clamp. */
+int iw_linear8_requant(const int32_t *acc, const uint32_t *multiplier, const int8_t *shift, int32_t *y, int64_t M,
+                       int64_t N, void *stream);
+
+/* rounding_rshift_debug -- pybind.cpp:22-43 (fixedpoint.h:47-87):
+ * y = rounding_rshift(x, shift) elementwise. */
+int iw_rounding_rshift(const int32_t *x, uint32_t shift, int32_t *y, int64_t numel, void *stream);
+
 /* linear32_{scalar,simd} -- linear32_scalar.cpp:96-129 (requant of
  * linear32_simd.cpp:231-255); pybind.cpp:82-101. -> y [M,N] int32. */
 int iw_linear32(const int8_t *x, const int8_t *weight, const int32_t *bias, const int8_t *weight_zero,

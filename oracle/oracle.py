@@ -121,6 +121,25 @@ class OracleLib:
                             _ptr(_c(mult, np.uint32)), _ptr(_c(shift, np.int8)), _ptr(y), M, K, N)
         return y
 
+    def linear8_requant(self, acc, mult, shift):
+        """linear8_requant_scalar (linear8_scalar.cpp:130-150): int32
+        rrs(mulh(acc, m[n]), (u32)s[n]), no clamp. Port library only."""
+        acc = _c(acc, np.int32)
+        N = acc.shape[-1]
+        y = np.empty(acc.shape, np.int32)
+        f = self.lib.iwo_linear8_requant
+        f.argtypes, f.restype = [_P, _P, _P, _P, _I64, _I64], None
+        f(_ptr(acc), _ptr(_c(mult, np.uint32)), _ptr(_c(shift, np.int8)), _ptr(y), acc.size // N, N)
+        return y
+
+    def rounding_rshift(self, x, shift):
+        """fixedpoint::rounding_rshift (common/fixedpoint.h:47-87) elementwise.
+        Port library only."""
+        x = _c(x, np.int32)
+        f = self.lib.iwo_rounding_rshift
+        f.argtypes, f.restype = [C.c_int32, C.c_uint32], C.c_int32
+        return np.array([f(int(v), int(shift)) for v in x.reshape(-1)], np.int32).reshape(x.shape)
+
     def residual15(self, branch, residual, mult):
         b = _c(branch, np.int32); r = _c(residual, np.int16)
         y = np.empty(r.shape, np.int16)

@@ -177,7 +177,7 @@ def test_rsqrt(ops, L):
     rng = np.random.default_rng(1)
     v = np.array(sorted(vals) + list(rng.integers(0, 1_000_000_001, 257)), np.int32)
     assert np.array_equal(host(ops.layernorm32_rsqrt_cuda(dev(v))), L.fisr(v, 13))
-    with pytest.raises(ValueError):
+    with pytest.raises(RuntimeError):  # TORCH_CHECK in the reference
         ops.layernorm32_rsqrt_cuda(dev(np.array([1, -1], np.int32)))
 
 
@@ -380,6 +380,30 @@ def test_accumulator_mirrors(ops, L):
     x, w, b, wz, _, _ = rand_linear(rng, 33, 100, 70)
     got = ops.linear32_accum_cuda_debug(dev(x), dev(w), dev(b), dev(wz))
     assert np.array_equal(host(got), L.linear8_accum(x, w, b, wz))
+
+
+def test_requant_debug_mirrors(ops, L):
+    """Requantise-only debug ops: linear8 requant (no clamp) and
+    rounding_rshift through their elementwise kernel, linear32 requant
+    through one bias-only GEMM row per input row."""
+    rng = np.random.default_rng(31)
+    acc = rng.integers(-(2 ** 31), 2 ** 31, (3, 5, 37), dtype=np.int64).astype(np.int32)
+    acc.reshape(-1)[:6] = [0, 1, -1, 2 ** 31 - 1, -(2 ** 31), 1234567]
+    m = rng.integers(0, 2 ** 32, 37, dtype=np.uint32)
+    m[:3] = [0x80000000, 0xFFFFFFFF, 0]
+    s = rng.integers(-3, 40, 37).astype(np.int8)
+    s[:4] = [0, 1, 31, 32]
+    got8 = ops.linear8_requant_cuda_debug(dev(acc), dev(m), dev(s))
+    assert got8.dtype == torch.int32 and np.array_equal(host(got8), L.linear8_requant(acc, m, s))
+    flat = acc.reshape(-1, 37)
+    want32 = np.stack([L.linear32(np.zeros((1, 16), np.int8), np.zeros((37, 16), np.int8), r, None, m, s)[0]
+                       for r in flat]).reshape(acc.shape)
+    got32 = ops.linear32_requant_cuda_debug(dev(acc), dev(m), dev(s))
+    assert np.array_equal(host(got32), want32)
+    x = rng.integers(-(2 ** 31), 2 ** 31, 4099, dtype=np.int64).astype(np.int32)
+    for sh in (0, 1, 7, 31, 32, 40):
+        got = ops.rounding_rshift_debug_cuda(dev(x), torch.tensor([sh], dtype=torch.uint32))
+        assert np.array_equal(host(got), L.rounding_rshift(x, sh)), sh
 
 
 def test_error_paths(ops):
