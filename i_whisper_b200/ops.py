@@ -159,10 +159,15 @@ def linear32_requant_cuda_debug(input, multiplier, shift):
 
 def rounding_rshift_debug_cuda(x, shift):
     """``_C.rounding_rshift_debug`` (pybind.cpp:22-43): fixedpoint
-    rounding_rshift of every int32 element by shift[0] (uint32)."""
-    _chk(x, "x", "int32"); _chk(shift, "shift", "uint32")
+    rounding_rshift of every int32 element by shift[0] (uint32). The shift is
+    read on the host, so its tensor may live on either device."""
+    _chk(x, "x", "int32")
+    if not isinstance(shift, torch.Tensor) or shift.dtype != torch.uint32:
+        raise RuntimeError("shift must be a uint32 tensor")
+    if shift.numel() < 1:
+        raise RuntimeError("shift must have at least one element")
     y = torch.empty_like(x)
-    _lib.call("iw_rounding_rshift", x.data_ptr(), _scalar(shift.reshape(-1)[:1], "shift"), y.data_ptr(), x.numel(),
+    _lib.call("iw_rounding_rshift", x.data_ptr(), int(shift.reshape(-1)[0].item()), y.data_ptr(), x.numel(),
               _stream())
     return y
 
