@@ -5,6 +5,8 @@ vcsd-lab/I-Whisper): seeded random inputs, tails that are not multiples of
 the tile sizes, shift edge cases, multipliers up to 0xFFFFFFFF, masks, and
 the BASELINE microbench shapes at reduced M.
 """
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -380,6 +382,80 @@ def test_accumulator_mirrors(ops, L):
     x, w, b, wz, _, _ = rand_linear(rng, 33, 100, 70)
     got = ops.linear32_accum_cuda_debug(dev(x), dev(w), dev(b), dev(wz))
     assert np.array_equal(host(got), L.linear8_accum(x, w, b, wz))
+
+
+CANARY, PAD = 0x5A, 512
+
+
+def _pitched_out(rows, ld, itemsize):
+    """A canary-filled byte buffer holding a rows x ld output (ld elements of
+    itemsize bytes per row) PAD bytes in; returns (buffer, output address)."""
+    buf = torch.full((2 * PAD + rows * ld * itemsize,), CANARY, dtype=torch.uint8, device="cuda")
+    return buf, buf.data_ptr() + PAD
+
+
+def _unpitch(buf, rows, cols, ld, dtype):
+    """Check every canary byte (before, after, and between rows past column
+    cols) and return the rows x cols output."""
+    h = host(buf)
+    isz = np.dtype(dtype).itemsize
+    assert (h[:PAD] == CANARY).all() and (h[PAD + rows * ld * isz:] == CANARY).all()
+    body = h[PAD:PAD + rows * ld * isz].reshape(rows, ld * isz)
+    assert (body[:, cols * isz:] == CANARY).all()
+    return np.ascontiguousarray(body[:, :cols * isz]).view(dtype)
+
+
+@pytest.mark.parametrize("form", ["l8_gelu_table", "l8_odd_pitch", "l32_res", "l32", "acc32"])
+def test_gemm_writes_only_its_output(ops, L, form):
+    """Canary-padded outputs at a row pitch wider than N: each GEMM form
+    writes exactly its M x N elements (ragged M and N tiles) and no byte
+    before, after or between the rows."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    M, K, N = 515, 256, 1000
+    rng = np.random.default_rng(zlib.crc32(form.encode()))
+    x, w, b, wz, m, s = rand_linear(rng, M, K, N, shift_lo=0, shift_hi=12 if form.startswith("l32") else 33)
+    X, W, B_, Z, Mu, S_ = dev(x), dev(w), dev(b), dev(wz), dev(m), dev(s)
+    rs = dev(x.astype(np.int32).sum(1).astype(np.int32))
+    st = torch.cuda.current_stream().cuda_stream
+    d = _lib.GemmDesc()
+    d.x, d.ldx, d.w, d.ldw, d.M, d.N, d.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    d.bias, d.weight_zero, d.x_rowsum, d.multiplier, d.shift = B_.data_ptr(), Z.data_ptr(), rs.data_ptr(), Mu.data_ptr(), S_.data_ptr()
+    keep = []
+    if form == "l8_gelu_table":
+        ld, dt, mode = 1040, np.int8, _lib.IW_GEMM_INT8
+        lut = rng.integers(0, 256, 16, dtype=np.uint8)
+        mi = rng.integers(0, 256, N, dtype=np.uint8); si = rng.integers(-2, 34, N).astype(np.int8)
+        mo = rng.integers(0, 256, N, dtype=np.uint8); so = rng.integers(-2, 34, N).astype(np.int8)
+        gp = [dev(a) for a in (lut, mi, si, mo, so)]
+        tab = torch.empty(N, 256, dtype=torch.int8, device="cuda")
+        _lib.call("iw_gelu_table", *[t.data_ptr() for t in gp], N, N, N, tab.data_ptr(), st)
+        tt = torch.empty((N + 127) // 128, 32768, dtype=torch.int8, device="cuda")
+        _lib.call("iw_gelu_table_tiled", tab.data_ptr(), N, tt.data_ptr(), st)
+        d.gelu_table, d.gelu_table_tiled = tab.data_ptr(), tt.data_ptr()
+        keep += gp + [tab, tt]
+        ref = L.gelu(L.linear8(x, w, b, wz, m, s), lut, mi, si, mo, so)
+    elif form == "l8_odd_pitch":
+        ld, dt, mode = 1037, np.int8, _lib.IW_GEMM_INT8
+        ref = L.linear8(x, w, b, wz, m, s)
+    elif form == "l32_res":
+        ld, dt, mode = N + 8, np.int16, _lib.IW_GEMM_LINEAR32_RES
+        r = rng.integers(-16383, 16384, (M, N), dtype=np.int16)
+        R = dev(r)
+        keep.append(R)
+        d.residual, d.ldr, d.residual_multiplier = R.data_ptr(), N, 40000
+        ref = L.residual15(L.linear32(x, w, b, wz, m, s), r, 40000)
+    elif form == "l32":
+        ld, dt, mode = N + 5, np.int32, _lib.IW_GEMM_LINEAR32
+        ref = L.linear32(x, w, b, wz, m, s)
+    else:
+        ld, dt, mode = N + 3, np.int32, _lib.IW_GEMM_ACC32
+        d.multiplier = d.shift = None
+        ref = L.linear8_accum(x, w, b, wz)
+    buf, out = _pitched_out(M, ld, np.dtype(dt).itemsize)
+    d.mode, d.out, d.ldo = mode, out, ld
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(d), st))
+    assert np.array_equal(_unpitch(buf, M, N, ld, dt), ref)
 
 
 def test_requant_debug_mirrors(ops, L):
