@@ -458,6 +458,50 @@ def test_gemm_writes_only_its_output(ops, L, form):
     assert np.array_equal(_unpitch(buf, M, N, ld, dt), ref)
 
 
+@pytest.mark.parametrize("path,B,H,Tq,Tk,mode", [("cc", 2, 3, 1, 300, 0), ("cc", 2, 2, 3, 3, 1), ("cc", 1, 2, 5, 1500, 0),
+                                                ("tc", 2, 4, 130, 130, 0)])
+def test_attention_writes_only_its_output(ops, L, path, B, H, Tq, Tk, mode):
+    """Canary-padded attention outputs at a row pitch wider than H*64: the
+    CUDA-core (decode, prefill) and tensor-core (encoder) kernels write
+    exactly the B x Tq x H*64 output."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    rng = np.random.default_rng(B * 100 + Tq * 10 + Tk)
+    d = H * 64
+    q = rng.integers(-127, 128, (B, Tq, d), dtype=np.int8)
+    k = rng.integers(-127, 128, (B, Tk, d), dtype=np.int8)
+    v = rng.integers(-127, 128, (B, Tk, d), dtype=np.int8)
+    P = {"a.qk_req_multiplier": np.array([90], np.uint8), "a.qk_req_shiftmount": np.array([10], np.int8),
+         "a.qk_frac_bits": np.array(7, np.int32), "a.av_req_multiplier": np.array([200], np.uint8),
+         "a.av_req_shiftmount": np.array([8], np.int8)}
+    mask = np.triu(np.ones((Tk, Tk), np.uint8), 1) if mode == 1 else None
+    ref = O.attention_core(L, P, "a", q, k, v, H, mask).reshape(B * Tq, d)
+    ldy = d + 64
+    buf, y = _pitched_out(B * Tq, ldy, 1)
+    Q, Kt, Vt = dev(q), dev(k), dev(v)
+    st = torch.cuda.current_stream().cuda_stream
+    if path == "cc":
+        _lib.call("iw_attention", Q.data_ptr(), d, Tq * d, Kt.data_ptr(), d, Tk * d, Vt.data_ptr(), d, Tk * d,
+                  y, ldy, Tq * ldy, B, H, Tq, Tk, mode, None, 90, 10, 7, 200, 8, 16, st)
+    else:
+        tab = torch.empty(32772, dtype=torch.uint8, device="cuda")
+        _lib.call("iw_shift_exp_table", 7, tab.data_ptr(), st)
+        vt_ld = (Tk + 15) // 16 * 16
+        vtb = torch.empty(B * H * 64, vt_ld, dtype=torch.int8, device="cuda")
+        a = _lib.AttnDesc()
+        a.q, a.ldq, a.q_bs, a.q_hs = Q.data_ptr(), d, Tq * d, 64
+        a.k, a.ldk, a.k_bs, a.k_hs = Kt.data_ptr(), d, Tk * d, 64
+        a.v, a.ldv, a.v_bs, a.v_hs = Vt.data_ptr(), d, Tk * d, 64
+        a.y, a.ldy, a.y_bs, a.y_hs = y, ldy, Tq * ldy, 64
+        a.B, a.H, a.Tq, a.Tk = B, H, Tq, Tk
+        a.qk_multiplier, a.qk_shift, a.frac_bits = 90, 10, 7
+        a.av_multiplier, a.av_shift, a.rsqrt_offset = 200, 8, 16
+        a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vtb.data_ptr(), vt_ld
+        _lib.check(_lib.LIB.iw_attention_ex(ctypes.byref(a), st))
+    assert np.array_equal(_unpitch(buf, B * Tq, d, ldy, np.int8), ref)
+    assert _lib.device_status(clear=True) == 0
+
+
 def test_requant_debug_mirrors(ops, L):
     """Requantise-only debug ops: linear8 requant (no clamp) and
     rounding_rshift through their elementwise kernel, linear32 requant
