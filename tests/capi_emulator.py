@@ -124,6 +124,8 @@ class CapiEmulator:
 
     def iw_layernorm64_stats(self, x, mean, var, rows, d, st):
         self._ln_width(d)
+        if rows < 0 or rows > 2 ** 31 - 1:
+            _fail(_lib.IW_EINVAL, "iw_layernorm64_stats: invalid row count")
         self.f["layernorm64_stats"](x, mean, var, rows, d)
 
     def iw_layernorm32_rsqrt(self, var, inv, n, st):
