@@ -9,7 +9,7 @@ and gathering the token matrices back in global utterance order.
 from __future__ import annotations
 
 import time
-from typing import List, Optional, Tuple
+from typing import List, Tuple
 
 
 def shard_bounds(n_total: int, world: int, rank: int) -> Tuple[int, int]:
