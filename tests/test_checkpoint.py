@@ -100,3 +100,18 @@ def test_config_format_checks(tiny, tmp_path):
         ck.load_int_checkpoint("no-such-size", root=str(tmp_path))
     with pytest.raises(RuntimeError, match="Expected model.safetensors"):
         ck.load_int_checkpoint(cfg_p)
+
+
+REF = os.environ.get("IWHISPER_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "i_whisper")), reason="reference checkout not available")
+def test_checkpoints_interchange_with_the_reference(tmp_path):
+    """Our saver's output loads in the reference's load_int_model, and the
+    reference's save_int_model output loads here, bit for bit (child process:
+    the reference import installs module stubs)."""
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, os.path.join(HERE, "reference_checkpoint_interop.py"), REF, str(tmp_path)],
+                       capture_output=True, text=True, timeout=600, env=dict(os.environ, PYTHONDONTWRITEBYTECODE="1"))
+    assert r.returncode == 0 and "interop ok" in r.stdout, r.stderr[-3000:]
