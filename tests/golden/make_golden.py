@@ -39,6 +39,9 @@ from i_whisper_b200.synthetic import synthetic_mel_batch  # noqa: E402
 GOLDEN_CASES = {
     # reduced-depth model with the full audio context and vocabulary
     "mini": dict(dims=ModelDims(80, 1500, 384, 6, 2, 51865, 448, 384, 6, 2), seed=0, mel_seeds=[1], sample_len=24),
+    # large's widths: 128 mel bins, d = 1280 (20 heads), the 51866-token vocabulary; one layer each side
+    "large1": dict(dims=ModelDims(128, 1500, 1280, 20, 1, 51866, 448, 1280, 20, 1), seed=6, mel_seeds=[9],
+                   sample_len=6),
 }
 
 
