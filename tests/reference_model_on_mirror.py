@@ -2,13 +2,13 @@
 repository's operator mirror as its ``_C`` (test helper, run as a script).
 
 Builds the reference model exactly as tests/golden/make_golden.py does
-(mini config, synthetic checkpoint, every module on the ``scalar``
+(one of its golden cases, synthetic checkpoint, every module on the ``scalar``
 backend), but with ``i_whisper.kernels._C.<op>_scalar`` served by
 ``i_whisper_b200.ops.<op>_cuda`` over the C-ABI emulator
 (capi_emulator.py) instead of the reference's compiled kernels. Prints one
 JSON object with the same digests and token ids as model_golden.json.
 
-Usage: python tests/reference_model_on_mirror.py REFERENCE_ROOT
+Usage: python tests/reference_model_on_mirror.py REFERENCE_ROOT [CASE]
 """
 import json
 import os
@@ -21,9 +21,10 @@ import capi_emulator  # noqa: E402
 import reference_suite_plugin as plugin  # noqa: E402
 
 capi_emulator.install(lambda obj, name, value: setattr(obj, name, value))
+CASE = sys.argv[2] if len(sys.argv) > 2 else "mini"
 sys.argv = [sys.argv[0], sys.argv[1]]  # make_golden reads the reference root from argv
 import make_golden as G  # noqa: E402
 
 G._bridge_C = plugin._make_C
 MI, ML, DEC = G.import_reference()
-print(json.dumps(G.run_reference(MI, ML, DEC, G.GOLDEN_CASES["mini"], "scalar")))
+print(json.dumps(G.run_reference(MI, ML, DEC, G.GOLDEN_CASES[CASE], "scalar")))

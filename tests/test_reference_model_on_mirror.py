@@ -1,6 +1,6 @@
 """The operator mirror as a drop-in ``_C`` under the reference's own model.
 
-A child process builds the reference ``Whisper_int`` (mini config) and runs
+A child process builds the reference ``Whisper_int`` (each golden case) and runs
 its encoder and its ``DecodingTask`` greedy loop with every ``_C.<op>_scalar``
 call served by ``i_whisper_b200.ops`` (argument checks, shapes and dtypes of
 the product; arithmetic of the oracle behind the emulated C ABI), and must
@@ -21,11 +21,15 @@ pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "i_whisper")
                                 reason="reference checkout not available")
 
 
-def test_reference_model_runs_on_the_mirror():
-    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "reference_model_on_mirror.py"), REF],
+GOLDEN = os.path.join(ROOT, "tests", "golden", "model_golden.json")
+
+
+@pytest.mark.parametrize("case", list(json.load(open(GOLDEN))))
+def test_reference_model_runs_on_the_mirror(case):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "reference_model_on_mirror.py"), REF, case],
                        capture_output=True, text=True, timeout=900, env=dict(os.environ, PYTHONDONTWRITEBYTECODE="1"))
     assert r.returncode == 0, r.stderr[-3000:]
     got = json.loads(r.stdout.strip().splitlines()[-1])
-    gold = json.load(open(os.path.join(ROOT, "tests", "golden", "model_golden.json")))["mini"]
+    gold = json.load(open(GOLDEN))[case]
     for key in ("mel_sha256", "encoder_sha256", "block_sha256", "tokens"):
         assert got[key] == gold[key], key
