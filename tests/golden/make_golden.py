@@ -79,17 +79,20 @@ def _bridge_C():
     return C
 
 
-def import_reference():
+def import_reference(ref: str = None, bridge=None):
+    """Import the reference's model_int, modules.linear and decoding with
+    ``_C`` served by ``bridge()`` (default: the reference scalar kernels)."""
+    ref = ref or REF
     for name in ("bitsandbytes", "bitsandbytes.functional", "matplotlib", "matplotlib.pyplot", "librosa"):
         sys.modules.setdefault(name, types.ModuleType(name))
     sys.modules["bitsandbytes"].functional = sys.modules["bitsandbytes.functional"]
     sys.modules["bitsandbytes.functional"].int8_linear_matmul = None
     sys.modules["matplotlib"].pyplot = sys.modules["matplotlib.pyplot"]
     kern = types.ModuleType("i_whisper.kernels")
-    kern._C = _bridge_C()
+    kern._C = (bridge or _bridge_C)()
     sys.modules["i_whisper.kernels"] = kern
     sys.modules["i_whisper.kernels._C"] = kern._C
-    sys.path.insert(0, REF)
+    sys.path.insert(0, ref)
     import i_whisper.model_int as MI
     import i_whisper.modules.linear as ML
     import i_whisper.decoding as DEC

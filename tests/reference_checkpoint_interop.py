@@ -19,11 +19,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path[:0] = [os.path.join(HERE, "golden"), os.path.dirname(HERE)]
 ref_root, work = sys.argv[1], sys.argv[2]
-sys.argv = [sys.argv[0], ref_root]  # make_golden reads the reference root from argv
 import make_golden as G  # noqa: E402
 from i_whisper_b200 import checkpoint as ck  # noqa: E402
 
-G.import_reference()
+G.import_reference(ref_root)
 import i_whisper  # noqa: E402  (the reference package, with its stubs in place)
 
 dims = ck.DIMS["tiny"]

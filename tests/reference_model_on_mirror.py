@@ -21,10 +21,8 @@ import capi_emulator  # noqa: E402
 import reference_suite_plugin as plugin  # noqa: E402
 
 capi_emulator.install(lambda obj, name, value: setattr(obj, name, value))
-CASE = sys.argv[2] if len(sys.argv) > 2 else "mini"
-sys.argv = [sys.argv[0], sys.argv[1]]  # make_golden reads the reference root from argv
+REF, CASE = sys.argv[1], (sys.argv[2] if len(sys.argv) > 2 else "mini")
 import make_golden as G  # noqa: E402
 
-G._bridge_C = plugin._make_C
-MI, ML, DEC = G.import_reference()
+MI, ML, DEC = G.import_reference(REF, bridge=plugin._make_C)
 print(json.dumps(G.run_reference(MI, ML, DEC, G.GOLDEN_CASES[CASE], "scalar")))

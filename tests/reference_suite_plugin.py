@@ -59,18 +59,9 @@ def _make_C():
 
 
 def _install_reference():
-    ref = os.environ["IWHISPER_REFERENCE"]
-    for name in ("bitsandbytes", "bitsandbytes.functional", "matplotlib", "matplotlib.pyplot", "librosa"):
-        sys.modules.setdefault(name, types.ModuleType(name))
-    sys.modules["bitsandbytes"].functional = sys.modules["bitsandbytes.functional"]
-    sys.modules["bitsandbytes.functional"].int8_linear_matmul = None
-    sys.modules["matplotlib"].pyplot = sys.modules["matplotlib.pyplot"]
-    C = _make_C()
-    kern = types.ModuleType("i_whisper.kernels")
-    kern._C = C
-    sys.modules["i_whisper.kernels"] = kern
-    sys.modules["i_whisper.kernels._C"] = C
-    sys.path.insert(0, ref)
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_golden
+    make_golden.import_reference(os.environ["IWHISPER_REFERENCE"], bridge=_make_C)
 
 
 def pytest_configure(config):
