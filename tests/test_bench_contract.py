@@ -45,3 +45,13 @@ def test_reference_arm_other_ranks_exit_quietly():
     r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_encoder_work_formula_matches_the_published_table():
+    """enc_gop (the roofline's algorithmic work per window) reproduces the
+    per-size figures 36.9 / 344.2 / 1138.1 / 2273.8 GOP."""
+    sys.path.insert(0, ROOT)
+    import bench
+    from i_whisper_b200.checkpoint import DIMS
+    for name, gop in bench.ENC_GOP.items():
+        assert round(bench.enc_gop(DIMS[name]), 1) == gop, name
