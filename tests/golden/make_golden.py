@@ -12,7 +12,8 @@ into the reference model with ``load_state_dict(strict=True)``; the input is
 the deterministic synthetic INT8 mel. The same run is repeated with every
 module on the ``torch`` golden backend as a cross-check.
 
-Writes tests/golden/model_golden.json (digests of the encoder output and
+Writes tests/golden/model_golden.json and, for the LayerNorm64 research
+variant, model_golden_ln64.json (digests of the encoder output and
 of each block's INT15 stream, plus the greedy token ids). Needs the
 reference checkout and oracle/_ref (``make -C oracle ref``).
 
@@ -44,6 +45,13 @@ GOLDEN_CASES = {
                    sample_len=6),
 }
 
+# the LayerNorm64 research variant (set_layernorm_backend "scalar64" / "torch64"),
+# kept in its own file: model_golden_ln64.json
+GOLDEN_CASES_LN64 = {
+    "mini_ln64": dict(dims=ModelDims(80, 1500, 384, 6, 2, 51865, 448, 384, 6, 2), seed=0, mel_seeds=[1],
+                      sample_len=24, layernorm="64"),
+}
+
 
 def sha(a) -> str:
     a = a.numpy() if isinstance(a, torch.Tensor) else np.asarray(a)
@@ -60,6 +68,7 @@ def _bridge_C():
     C.linear32_scalar = lambda x, w, b, z, m, s: t(R.linear32(n(x), n(w), n(b), n(z), n(m), n(s)))
     C.residual15_scalar = lambda br, r, m: t(R.residual15(n(br), n(r), n(m)))
     C.layernorm32_scalar = lambda x, g, b, lm, ls, om, os_: t(R.layernorm32(n(x), n(g), n(b), n(lm), n(ls), n(om), n(os_)))
+    C.layernorm64_scalar = lambda x, g, b, lm, ls, om, os_: t(R.layernorm64(n(x), n(g), n(b), n(lm), n(ls), n(om), n(os_)))
     C.gelu_scalar = lambda x, lut, mi, si, mo, so: t(R.gelu(n(x), n(lut), n(mi), n(si), n(mo), n(so)))
 
     def qk(q, k, mask, m, s):
@@ -111,6 +120,8 @@ def run_reference(MI, ML, DEC, case, backend):
                MI.set_conv1d_backend, MI.set_audio_encoder_backend, MI.set_text_decoder_backend,
                ML.set_linear8_backend, ML.set_linear32_backend):
         fn(model, backend, logger=quiet)
+    if case.get("layernorm") == "64":
+        MI.set_layernorm_backend(model, backend + "64", logger=quiet)
     model.eval()
     mel = torch.from_numpy(synthetic_mel_batch(dims.n_mels, case["mel_seeds"], float(sd["encoder.input_alpha"][0])))
     blocks = {}
@@ -130,16 +141,19 @@ def run_reference(MI, ML, DEC, case, backend):
 
 def main():
     MI, ML, DEC = import_reference()
-    out = {}
-    for name, case in GOLDEN_CASES.items():
-        res = run_reference(MI, ML, DEC, case, "scalar")
-        res_t = run_reference(MI, ML, DEC, case, "torch")
-        assert res == res_t, "reference scalar and torch backends disagree"
-        out[name] = dict(dims=case["dims"].__dict__, seed=case["seed"], mel_seeds=case["mel_seeds"],
-                         sample_len=case["sample_len"], **res)
-        print(name, res["encoder_sha256"][:16], res["tokens"])
-    with open(os.path.join(HERE, "model_golden.json"), "w") as f:
-        json.dump(out, f, indent=1)
+    for cases, fname in ((GOLDEN_CASES, "model_golden.json"), (GOLDEN_CASES_LN64, "model_golden_ln64.json")):
+        out = {}
+        for name, case in cases.items():
+            res = run_reference(MI, ML, DEC, case, "scalar")
+            res_t = run_reference(MI, ML, DEC, case, "torch")
+            assert res == res_t, "reference scalar and torch backends disagree"
+            out[name] = dict(dims=case["dims"].__dict__, seed=case["seed"], mel_seeds=case["mel_seeds"],
+                             sample_len=case["sample_len"], **res)
+            if case.get("layernorm"):
+                out[name]["layernorm"] = case["layernorm"]
+            print(name, res["encoder_sha256"][:16], res["tokens"])
+        with open(os.path.join(HERE, fname), "w") as f:
+            json.dump(out, f, indent=1)
 
 
 if __name__ == "__main__":

@@ -25,4 +25,5 @@ REF, CASE = sys.argv[1], (sys.argv[2] if len(sys.argv) > 2 else "mini")
 import make_golden as G  # noqa: E402
 
 MI, ML, DEC = G.import_reference(REF, bridge=plugin._make_C)
-print(json.dumps(G.run_reference(MI, ML, DEC, G.GOLDEN_CASES[CASE], "scalar")))
+cases = dict(G.GOLDEN_CASES, **G.GOLDEN_CASES_LN64)
+print(json.dumps(G.run_reference(MI, ML, DEC, cases[CASE], "scalar")))

@@ -21,15 +21,16 @@ pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "i_whisper")
                                 reason="reference checkout not available")
 
 
-GOLDEN = os.path.join(ROOT, "tests", "golden", "model_golden.json")
+GOLDENS = [os.path.join(ROOT, "tests", "golden", f) for f in ("model_golden.json", "model_golden_ln64.json")]
+CASES = [(p, c) for p in GOLDENS for c in json.load(open(p))]
 
 
-@pytest.mark.parametrize("case", list(json.load(open(GOLDEN))))
-def test_reference_model_runs_on_the_mirror(case):
+@pytest.mark.parametrize("path,case", CASES, ids=[c for _, c in CASES])
+def test_reference_model_runs_on_the_mirror(path, case):
     r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "reference_model_on_mirror.py"), REF, case],
                        capture_output=True, text=True, timeout=900, env=dict(os.environ, PYTHONDONTWRITEBYTECODE="1"))
     assert r.returncode == 0, r.stderr[-3000:]
     got = json.loads(r.stdout.strip().splitlines()[-1])
-    gold = json.load(open(GOLDEN))[case]
+    gold = json.load(open(path))[case]
     for key in ("mel_sha256", "encoder_sha256", "block_sha256", "tokens"):
         assert got[key] == gold[key], key
