@@ -1,14 +1,16 @@
 """The oracle's greedy filter chain against the reference's own logit
 filters (test helper, run as a script).
 
-Builds SuppressBlank, SuppressTokens and ApplyTimestampRules from the
-reference's i_whisper/decoding.py (:426-510) in the order DecodingTask
-installs them (:556-572), with a stand-in tokenizer that carries the
-special-token ids of i_whisper_b200/assets/decode_tokens.json, and applies
-them and ``oracle.apply_filters_torch`` to the same float logits for token
-histories of every kind (text, timestamps, pairs, EOT; 0-5 sampled tokens,
-with and without a dominant timestamp block). The filtered logits must be
-identical. Prints "filters ok".
+Builds the reference's own DecodingTask (i_whisper/decoding.py:517-632,
+``language="en"``, greedy) for each vocabulary size and checks that its
+tokenizer ids, SOT sequence, blank tokens, SuppressTokens set and
+max_initial_timestamp index are those of i_whisper_b200/assets/
+decode_tokens.json; then applies the task's own logit filters
+(SuppressBlank, SuppressTokens, ApplyTimestampRules, :426-510) and
+``oracle.apply_filters_torch`` to the same float logits for token histories
+of every kind (text, timestamps, pairs, EOT; 0-5 sampled tokens, with and
+without a dominant timestamp block). The filtered logits must be identical.
+Prints "filters ok".
 
 Usage: python tests/reference_filters_check.py REFERENCE_ROOT
 """
@@ -25,18 +27,25 @@ import make_golden as G  # noqa: E402
 from oracle import oracle as O  # noqa: E402
 from i_whisper_b200.model import decode_tokens  # noqa: E402
 
-_, _, DEC = G.import_reference(sys.argv[1], bridge=lambda: types.ModuleType("_C"))
+MI, _, DEC = G.import_reference(sys.argv[1], bridge=lambda: types.ModuleType("_C"))
 
-for V in (51865, 51866):
+for V, n_mels in ((51865, 80), (51866, 128)):
     t = decode_tokens(V)
     tb, eot = t["timestamp_begin"], t["eot"]
-    tok = types.SimpleNamespace(eot=eot, no_timestamps=t["no_timestamps"], timestamp_begin=tb,
-                                encode=lambda s, blank=tuple(t["blank"]): list(blank) if s == " " else None)
+    # the reference's own DecodingTask (decoding.py:517-632) for this vocabulary
+    model = MI.Whisper_int(MI.ModelDimensions(n_mels, 1500, 384, 6, 1, V, 448, 384, 6, 1))
+    task = DEC.DecodingTask(model, DEC.DecodingOptions(fp16=False, language="en"))
+    tok = task.tokenizer
+    assert list(task.sot_sequence) == t["sot_sequence"] and task.sample_begin == len(t["sot_sequence"])
+    assert (tok.sot, tok.eot, tok.no_timestamps, tok.timestamp_begin) == (t["sot"], eot, t["no_timestamps"], tb)
+    assert tok.encode(" ") == t["blank"]
+    kinds = [type(f).__name__ for f in task.logit_filters]
+    assert kinds == ["SuppressBlank", "SuppressTokens", "ApplyTimestampRules"], kinds
+    assert sorted(task.logit_filters[1].suppress_tokens) == t["suppress"]
+    assert task.logit_filters[2].max_initial_timestamp_index == 50
     spec = O.DecodeTokens(sot=t["sot"], eot=eot, sot_sequence=t["sot_sequence"], no_timestamps=t["no_timestamps"],
                           timestamp_begin=tb, blank=t["blank"], suppress=t["suppress"])
-    Tp = len(t["sot_sequence"])
-    # max_initial_timestamp 1.0 s at 0.02 s per timestamp step (decoding.py:562-567)
-    filters = [DEC.SuppressBlank(tok, Tp), DEC.SuppressTokens(t["suppress"]), DEC.ApplyTimestampRules(tok, Tp, 50)]
+    Tp = task.sample_begin
     for n_hist in (0, 1, 2, 3, 5):
         rng = np.random.default_rng(V + n_hist)
         B = 48
@@ -50,7 +59,7 @@ for V in (51865, 51866):
                     eot if r < 0.55 else int(rng.integers(0, eot)))
         tokens = torch.from_numpy(np.concatenate([np.tile(np.array(t["sot_sequence"]), (B, 1)), hist], 1))
         ref = torch.from_numpy(logits.copy())
-        for f in filters:
+        for f in task.logit_filters:
             f.apply(ref, tokens)
         got = torch.from_numpy(logits.copy())
         O.apply_filters_torch(got, tokens, spec, Tp)
