@@ -1,8 +1,7 @@
-"""Every ``file:line`` citation of the reference in this repository's code,
-tests and design documents names a file that exists in the reference
-checkout and a line range inside it (the survey and baseline notes that the
-build started from are inputs, not checked here). Skipped when the
-reference checkout is absent."""
+"""Every ``file:line`` citation of the reference in this repository's code
+and tests (docstrings and comments) names a file that exists in the
+reference checkout and a line range inside it. Skipped when the reference
+checkout is absent."""
 import os
 import re
 import subprocess
@@ -12,8 +11,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.environ.get("IWHISPER_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 CITE = re.compile(r"([A-Za-z_][A-Za-z0-9_./-]*\.(?:py|cpp|h|hpp|csv|report|toml)):(\d+)(?:-(\d+))?")
-SOURCES = (".py", ".cu", ".cuh", ".h", ".c", ".cpp", ".md")
-INPUT_NOTES = {"SURVEY.md", "BASELINE.md"}
+SOURCES = (".py", ".cu", ".cuh", ".h", ".c", ".cpp")
 
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "i_whisper")),
                                 reason="reference checkout not available")
@@ -34,7 +32,7 @@ def test_citations_point_inside_reference_files():
     lines = {}
     bad, checked = [], 0
     for rel in tracked:
-        if not rel.endswith(SOURCES) or rel in INPUT_NOTES:
+        if not rel.endswith(SOURCES):
             continue
         text = open(os.path.join(ROOT, rel), errors="replace").read()
         for m in CITE.finditer(text):
