@@ -20,6 +20,12 @@ ResidualAttentionBlock_int.forward :1112-1177, MultiHeadAttention_int
 :713-1042, TextDecoder_int.forward :1398-1484) and the greedy loop of
 ``i_whisper/decoding.py`` (:684-712, filters :426-510, GreedyDecoder :280-296)
 over a state dict keyed exactly like ``Whisper_int.state_dict()``.
+
+Parity is pinned: the kernels against the reference's compiled scalar
+kernels and its own kernel test suite, the dataflow and greedy loop against
+golden digests and tokens that the reference's Whisper_int and DecodingTask
+produced (tests/golden), and the filter chain against the reference
+DecodingTask's own logit filters.
 """
 from __future__ import annotations
 
