@@ -4,9 +4,16 @@ Workload (per GPU): whisper-medium integer encoder
 over a batch of 256 synthetic 30 s windows (d_model 1024, 24 layers, 16
 heads, 80 mels), then greedy decoding of 128 tokens per window with an INT8
 self-attention KV cache and INT8 cross-attention over the 1500 encoder
-states. Weights are the deterministic synthetic checkpoint
-(``checkpoint.synthetic_state_dict``, seed 0); inputs are seeded sine+noise
+states. Weights are the reference-calibrated checkpoint the configuration
+names (random-init from seed 0, calibrated and quantised by the reference's
+own quantiser on 8 synthetic windows: CKPT/iwhisper-medium-calib-seed0, made
+by tests/golden/make_calibrated.py; the deterministic synthetic checkpoint
+when it is absent, which the line then says); inputs are seeded sine+noise
 windows through the float log-mel frontend (seeds recycled modulo 32).
+
+* ``parity``: outside the timed region, windows 0 and 1 of every rank's
+  batch (seeds 0 and 1) are compared with the committed golden digests of
+  the oracle (encoder output and the first 8 greedy tokens).
 
 * ``value``: encoder windows/s of the whole job (all ranks), inputs resident
   in HBM; one step = one encoder pass over the batch.
@@ -18,7 +25,10 @@ windows through the float log-mel frontend (seeds recycled modulo 32).
 * ``decoder``: greedy decoding tok/s (device-resident and end to end with
   the token matrix read back).
 * ``roofline``: the dominant kernel, achieved work per launch from CUDA
-  events over the timed steps.
+  events over the timed steps, against the dense INT8 tensor peak taken as
+  2 x the measured dense BF16 peak (MEASURED_PEAKS.json; INT8 runs at twice
+  the BF16 rate on B200), with the datasheet 4500 TOPS and an in-run
+  torch._int_mm probe reported beside it.
 * ``cpu_baseline``: the reference's own scalar C++ kernels (oracle/_ref) on a
   bounded sample of the same workload on the host cores (rank 0, N=1).
 
@@ -258,6 +268,47 @@ def traffic_per_launch(kernel: str, windows: int, dims):
     return None
 
 
+def load_golden(model: str, sd):
+    """The committed oracle digests for this model's calibrated checkpoint
+    (tests/golden/calibrated_golden.json), or None when the weights are not
+    the ones the digests were made with."""
+    from i_whisper_b200.checkpoint import state_digest
+    p = os.path.join(ROOT, "tests", "golden", "calibrated_golden.json")
+    if not os.path.exists(p):
+        return None
+    g = json.load(open(p))
+    key = {"medium": "medium_w2"}.get(model)
+    ck = g.get("checkpoints", {}).get(model)
+    if key not in g or not ck or ck["state_digest"] != state_digest(sd):
+        return None
+    return g[key]
+
+
+def check_parity(golden, xa, toks, seeds):
+    """Windows of this rank's batch whose seeds have golden digests: encoder
+    output bytes and the first greedy tokens against the oracle's."""
+    import hashlib
+    if golden is None:
+        return {"ok": False, "why": "no golden digests for these weights"}
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    checked, bad = [], []
+    for j, s in enumerate(golden["mel_seeds"]):
+        if s not in seeds:
+            continue
+        b = seeds.index(s)
+        enc_ok = sha(xa[b].cpu().numpy()) == golden["encoder_sha256"][j]
+        tok_ok = True
+        if toks is not None:
+            n = len(golden["tokens"][j])
+            tok_ok = toks[b, :n].cpu().numpy().tolist() == golden["tokens"][j]
+        checked.append(b)
+        if not (enc_ok and tok_ok):
+            bad.append({"window": b, "encoder": enc_ok, "tokens": tok_ok})
+    return {"ok": bool(checked) and not bad, "windows": checked, "mismatches": bad,
+            "against": "oracle digests, tests/golden/calibrated_golden.json (encoder output, "
+                       f"{golden['sample_len']} greedy tokens)"}
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -276,7 +327,7 @@ def main():
 
     import torch
     import torch.distributed as dist
-    from i_whisper_b200.checkpoint import DIMS, synthetic_state_dict
+    from i_whisper_b200.checkpoint import DIMS, calibrated_name, load_calibrated, synthetic_state_dict
     from i_whisper_b200.model import KernelTimer, WhisperIntB200
     from i_whisper_b200.sharding import max_over_ranks, shard_bounds, window_seeds
     from i_whisper_b200.synthetic import synthetic_mel_batch
@@ -297,14 +348,21 @@ def main():
             dist.all_reduce(t)
         torch.cuda.synchronize()
 
-    dims = DIMS[args.model]
     B = args.batch
-    sd = synthetic_state_dict(dims, seed=0)
+    try:
+        dims, sd = load_calibrated(args.model)
+        weights = "reference-calibrated checkpoint " + calibrated_name(args.model)
+    except FileNotFoundError:
+        dims = DIMS[args.model]
+        sd = synthetic_state_dict(dims, seed=0)
+        weights = "synthetic checkpoint (checkpoint.synthetic_state_dict, seed 0): calibrated one absent"
+    golden = load_golden(args.model, sd)
+    input_alpha = float(np.asarray(sd["encoder.input_alpha"]).reshape(-1)[0])
     model = WhisperIntB200(dims, sd)
     del sd
     start, stop = shard_bounds(B * world, world, rank)  # weak scaling: B utterances per rank
     seeds = window_seeds(start, stop)
-    mels32 = synthetic_mel_batch(dims.n_mels, sorted(set(seeds)), 100.0)
+    mels32 = synthetic_mel_batch(dims.n_mels, sorted(set(seeds)), input_alpha)
     mel_np = np.stack([mels32[s % len(mels32)] for s in seeds])
     mel = torch.from_numpy(mel_np).cuda()
     enc_gops = enc_gop(dims)
@@ -380,9 +438,17 @@ def main():
         dec_e2e_ms = max_over_ranks(g0.elapsed_time(g1), device="cuda")
         dec_e2e_tps = B * world * args.decode_tokens / (dec_e2e_ms / 1e3)
 
+    # ---- parity (outside the timed regions) -----------------------------------
+    parity = check_parity(golden, xa, toks if args.decode_runs > 0 else None, seeds)
+    ok = torch.tensor([1 if parity.get("ok") else 0], device="cuda")
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    parity["all_ranks_ok"] = bool(ok.item())
+
     # ---- roofline of the dominant kernel ------------------------------------
     peaks = measured_peaks()
-    int8_peak = int8_mm_peak(torch)
+    int8_probe = int8_mm_peak(torch)
+    int8_peak = 2.0 * peaks["bf16_tflops"]
     dom = max(ksum.items(), key=lambda kv: kv[1]["ms"])
     dname, dk = dom
     kernels = {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
@@ -393,7 +459,9 @@ def main():
         achieved = dk["ops"] / dk["launches"] / (dk["ms"] / dk["launches"] * 1e-3) / 1e12
         roof = {"kernel": dname, "bound": "tensor", "achieved": round(achieved, 2), "peak": round(int8_peak, 1),
                 "unit": "TFLOP/s", "frac": round(achieved / int8_peak, 4),
-                "peak_source": "measured torch._int_mm int8 8192^3 burst on this GPU (no INT8 entry in MEASURED_PEAKS.json)",
+                "peak_source": ("2 x MEASURED_PEAKS.json bf16_tflops (dense INT8 = 2 x dense BF16 on B200; "
+                                "the file has no INT8 entry)" + (" [fallback peaks]" if peaks.get("fallback") else "")),
+                "frac_of_int_mm_probe": round(achieved / int8_probe, 4), "int_mm_probe_tops": round(int8_probe, 1),
                 "frac_of_datasheet_4500": round(achieved / DATASHEET_INT8_TOPS, 4),
                 "traffic": traffic_per_launch(dname, B, dims), "traffic_unit": "bytes per launch",
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel family "
@@ -409,11 +477,14 @@ def main():
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "windows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded sine+noise windows; random-init synthetic checkpoint)",
+        "vs_baseline": None, "dtype": "int8", "data": f"synthetic (seeded sine+noise windows; {weights})",
         "config": arm_config(args, world),
         "pct_int8_tc_peak": {"encoder_tops": round(enc_tops, 1),
-                             "of_measured_int8_mm": round(enc_tops / int8_peak, 4),
+                             "of_2x_measured_bf16": round(enc_tops / int8_peak, 4),
+                             "of_int_mm_probe": round(enc_tops / int8_probe, 4),
                              "of_datasheet_4500": round(enc_tops / DATASHEET_INT8_TOPS, 4)},
+        "parity_checked": parity["all_ranks_ok"],
+        "parity": parity,
         "decoder": {"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
                     "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
                     "ms_per_decode": round(dec_ms / max(1, args.decode_runs), 2)},

@@ -10,6 +10,8 @@ sot_prev, sot_lm, no_speech). They depend only on the vocabulary size
 a checkout that has the reference, and shipped as data.
 
 Usage: python i_whisper_b200/assets/make_decode_tokens.py [REFERENCE_ROOT]
+(default: $IWHISPER_REFERENCE, else a checkout named ``reference`` next to
+this repository; it is an error when neither exists)
 """
 import json
 import os
@@ -17,7 +19,11 @@ import sys
 
 import types
 
-ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+_repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("IWHISPER_REFERENCE",
+                                                           os.path.join(os.path.dirname(_repo), "reference"))
+if not os.path.isdir(os.path.join(ref, "i_whisper")):
+    sys.exit(f"vcsd-lab/I-Whisper checkout not found at {ref!r}: pass its path or set IWHISPER_REFERENCE")
 # The reference package imports bitsandbytes, matplotlib and librosa at
 # import time; none is used by the tokenizer, so empty stand-ins suffice.
 for name in ("bitsandbytes", "bitsandbytes.functional", "matplotlib", "matplotlib.pyplot", "librosa"):

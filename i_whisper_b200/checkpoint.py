@@ -184,6 +184,52 @@ def save_int_checkpoint(dims: ModelDims, sd: Dict[str, np.ndarray], prefix: str,
     return d
 
 
+def state_digest(sd: Dict[str, np.ndarray]) -> str:
+    """sha256 over every tensor (sorted keys; name, dtype, shape and bytes):
+    identifies a checkpoint's content independently of file layout."""
+    import hashlib
+    h = hashlib.sha256()
+    for k in sorted(sd):
+        a = np.asarray(sd[k])
+        h.update(k.encode())
+        h.update(str(a.dtype).encode())
+        h.update(str(tuple(a.shape)).encode())
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+# ---------------------------------------------------------------------------
+# Reference-calibrated checkpoints (random-init float weights from seed 0,
+# calibrated and quantised by the reference's own quantiser on 8 synthetic
+# windows; generated by tests/golden/make_calibrated.py)
+# ---------------------------------------------------------------------------
+def ckpt_root() -> str:
+    """Checkpoint directory: $IWHISPER_CKPT, else CKPT/ in the repository."""
+    return os.environ.get("IWHISPER_CKPT") or os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                                           "CKPT")
+
+
+def calibrated_name(size: str) -> str:
+    return f"{size}-calib-seed0"
+
+
+def calibrated_path(size: str) -> str:
+    return os.path.join(ckpt_root(), f"iwhisper-{calibrated_name(size)}")
+
+
+def load_calibrated(size: str):
+    """(dims, state dict) of the reference-calibrated ``size`` checkpoint:
+    the full checkpoint when it is present, else rebuilt from its compact
+    record (calibrated.rebuild); FileNotFoundError when neither exists."""
+    p = calibrated_path(size)
+    if os.path.isfile(os.path.join(p, "model.safetensors")):
+        return load_int_checkpoint(p)
+    from .calibrated import rebuild, record_path
+    if os.path.isfile(record_path(size)):
+        return rebuild(record_path(size))
+    raise FileNotFoundError(f"{p}: run tests/golden/make_calibrated.py --sizes {size}")
+
+
 # ---------------------------------------------------------------------------
 # Deterministic synthetic checkpoint
 # ---------------------------------------------------------------------------

@@ -57,7 +57,11 @@ constexpr int OC = 64 / SLICES;       // output columns per warp
 constexpr int QK_WARP = 2 + SOFT_WARPS;  // the Q.K^T issuer
 constexpr int THREADS = 96 + 32 * SOFT_WARPS;
 static_assert(SC % 32 == 0 && (OC == 16 || OC == 32), "softmax warp split");
-constexpr int TAB_MAX = 4096;  // entries of the shift-exp table kept in shared memory
+// The whole shift-exp table lives in shared memory: its zero entry t1 is at
+// most 32769 (frac_bits >= 15 keeps non-zero values down to xs = -32768), so
+// the header (2 bytes) and t1 + 1 entries take at most 32772 bytes.
+constexpr int TAB_MAX = 32770;                    // entries (indices 0..32769)
+constexpr int TAB_SMEM = (2 + TAB_MAX + 15) / 16 * 16;  // header + entries, 16-byte chunks
 
 constexpr int Q_BYTES = BQ * 64;
 constexpr int K_BYTES = BK * 64;
@@ -140,7 +144,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     uint8_t *sP = smem + OFF_P;
     // the shift-exp table lives in static shared memory: its address is a
     // compile-time constant, so a lookup is one load with an immediate offset
-    __shared__ uint8_t sTab[TAB_MAX];
+    __shared__ __align__(16) uint8_t sTabRaw[TAB_SMEM];
+    uint8_t *const sTab = sTabRaw + 2;  // entry i at sTabRaw[2 + i], as in global memory
     int32_t *sRed = reinterpret_cast<int32_t *>(smem + OFF_RED);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *q_full = bars;                 // [2]
@@ -321,7 +326,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const int et = sw * 32 + lane;
         // index of the zero entry (bounded by the shared-memory table size)
         const uint32_t t1 = min((uint32_t)p.tab[0] | ((uint32_t)p.tab[1] << 8), (uint32_t)(TAB_MAX - 1));
-        for (uint32_t i = et; i <= t1; i += SOFT_WARPS * 32) sTab[i] = p.tab[2 + i];
+        {
+            // header and entries 0..t1 (t1 + 3 bytes): whole 16-byte chunks
+            // when the table is 16-byte aligned, then the tail bytes; never
+            // past byte t1 + 2 of the caller's buffer
+            const uint32_t nbytes = t1 + 3;
+            uint32_t done = 0;
+            if ((reinterpret_cast<uintptr_t>(p.tab) & 15u) == 0) {
+                const uint32_t n16 = nbytes / 16;
+                for (uint32_t i = et; i < n16; i += SOFT_WARPS * 32)
+                    reinterpret_cast<uint4 *>(sTabRaw)[i] = __ldg(reinterpret_cast<const uint4 *>(p.tab) + i);
+                done = n16 * 16;
+            }
+            for (uint32_t i = done + et; i < nbytes; i += SOFT_WARPS * 32) sTabRaw[i] = p.tab[i];
+        }
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t col = (uint32_t)(slice * SC);
         const RrsK k_rsq = rrs_k(p.rsqrt_offset), k_av = rrs_k(p.av_shift);  // output normalisation shifts
@@ -363,7 +381,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
                         asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
                     }
-                    rs = __dp4a((int32_t)ww, 0x01010101, rs);
+                    // probabilities are unsigned bytes (up to 255 for frac_bits >= 15)
+                    rs = (int32_t)__dp4a(ww, 0x01010101u, (uint32_t)rs);
                     w4[q4] = ww;
                 }
             } else {
@@ -663,18 +682,17 @@ cudaError_t attention_tc(const AttnArgs &a, int B, int H, const uint8_t *tab, in
     p.rsqrt_offset = a.rsqrt_offset;
     p.vt_ld = vt_ld;
     p.rowsum_out = a.rowsum_out;
-    static bool attr = false;
-    if (!attr) {
-        e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static SmemLimit lim_fast, lim_gen;
     const int items = B * H * ((T + BQ - 1) / BQ);
     const int grid = items < num_sms() ? items : num_sms();
     const bool fast = a.qk_mult >= 1 && a.qk_mult <= 255 && sh >= 1 && sh <= 31;
-    if (fast) return launch_pdl(attn_tc_kernel<true>, grid, THREADS, SMEM, st, tq, tk, tv, p);
+    if (fast) {
+        e = raise_smem_limit(attn_tc_kernel<true>, SMEM, lim_fast);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(attn_tc_kernel<true>, grid, THREADS, SMEM, st, tq, tk, tv, p);
+    }
+    e = raise_smem_limit(attn_tc_kernel<false>, SMEM, lim_gen);
+    if (e != cudaSuccess) return e;
     return launch_pdl(attn_tc_kernel<false>, grid, THREADS, SMEM, st, tq, tk, tv, p);
 }
 

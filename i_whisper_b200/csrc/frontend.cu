@@ -143,12 +143,9 @@ cudaError_t log_mel_int8(const float *audio, int B, int n_samples, int64_t lda, 
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t smem = logmel_smem_bytes(n_mels);
-    static size_t smem_set = 0;
-    if (smem > 48 * 1024 && smem > smem_set) {
-        e = cudaFuncSetAttribute(logmel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    static SmemLimit lim;
+    e = raise_smem_limit(logmel_kernel, smem, lim);
+    if (e != cudaSuccess) return e;
     dim3 grid((n_frames + kLmFrames - 1) / kLmFrames, B);
     e = launch_pdl(logmel_kernel, grid, kLmThreads, smem, st, audio, lda, n_samples, n_frames, filters, n_mels, work,
                    wmax);

@@ -639,12 +639,9 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
     else
         e = make_tmap_2d_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, BR);
     if (e != cudaSuccess) return e;
-    static bool attr_set = false;
-    if (!attr_set) {
-        e = cudaFuncSetAttribute(gemm_cm_kernel<BR, MODE, GK>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static SmemLimit lim;
+    e = raise_smem_limit(gemm_cm_kernel<BR, MODE, GK>, Cfg::SMEM, lim);
+    if (e != cudaSuccess) return e;
     const long row_tiles = g.win_rows > 0 ? (long)(g.M / g.win_rows) * ((g.win_rows + BR - 1) / BR)
                                           : (long)((g.M + BR - 1) / BR);
     const long tiles = (long)((g.N + 127) / 128) * row_tiles;

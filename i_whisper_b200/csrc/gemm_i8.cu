@@ -539,17 +539,6 @@ bool cm_enabled() {
     return on == 1;
 }
 
-int num_sms() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
-
 template <int BN, int MODE, int FLAVOR>
 static cudaError_t launch_t(const GemmShape &g, const EpiParams &p, cudaStream_t stream) {
     using Cfg = GemmCfg<BN, FLAVOR>;
@@ -558,13 +547,9 @@ static cudaError_t launch_t(const GemmShape &g, const EpiParams &p, cudaStream_t
     if (e != cudaSuccess) return e;
     e = make_tmap_2d_u8(&tb, g.w, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.ldw, kBlockK, BN);
     if (e != cudaSuccess) return e;
-    static bool attr_set = false;
-    if (!attr_set) {
-        e = cudaFuncSetAttribute(gemm_i8_kernel<BN, MODE, FLAVOR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg::SMEM);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    static SmemLimit lim;
+    e = raise_smem_limit(gemm_i8_kernel<BN, MODE, FLAVOR>, Cfg::SMEM, lim);
+    if (e != cudaSuccess) return e;
     const int tiles = ((g.M + kBlockM - 1) / kBlockM) * ((g.N + BN - 1) / BN);
     const int grid = tiles < num_sms() ? tiles : num_sms();
     return launch_pdl(gemm_i8_kernel<BN, MODE, FLAVOR>, grid, kThreads, Cfg::SMEM, stream, ta, tb, g.M, g.N, g.K, p);

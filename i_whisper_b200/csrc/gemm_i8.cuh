@@ -120,7 +120,4 @@ cudaError_t gemm_cm_launch(const GemmShape &g, EpiMode mode, const EpiParams &p,
 // row-major kernel for every GEMM; used to compare the two).
 bool cm_enabled();
 
-// Number of SMs of the current device (cached).
-int num_sms();
-
 }  // namespace iw

@@ -5,8 +5,10 @@
 // wrap-around behaviour is spelled out with uint32 arithmetic.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
+#include <mutex>
 #include <utility>
 #include <cuda_runtime.h>
 
@@ -168,6 +170,49 @@ inline bool pdl_enabled() {
         on = (e && e[0] == '0') ? 0 : 1;
     }
     return on == 1;
+}
+
+// Kernel attributes belong to a device's context: a process that drives
+// several GPUs must set them on each. SmemLimit records, per device, the
+// dynamic shared-memory limit already set for one kernel; raise_smem_limit
+// sets it on the current device the first time a launch there needs more.
+// The set-and-record runs under a mutex so that two host threads can never
+// leave a smaller limit in place than the one recorded.
+constexpr int kMaxDevices = 64;
+struct SmemLimit {
+    std::atomic<int> bytes[kMaxDevices];  // static storage: zero-initialised
+    std::mutex mu;
+};
+
+template <typename... KArgs>
+inline cudaError_t raise_smem_limit(void (*kernel)(KArgs...), size_t bytes, SmemLimit &lim) {
+    if (bytes <= 48 * 1024) return cudaSuccess;  // the default limit
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int want = (int)bytes;
+    if (dev < 0 || dev >= kMaxDevices)
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (lim.bytes[dev].load(std::memory_order_acquire) >= want) return cudaSuccess;
+    std::lock_guard<std::mutex> g(lim.mu);
+    if (lim.bytes[dev].load(std::memory_order_relaxed) >= want) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e == cudaSuccess) lim.bytes[dev].store(want, std::memory_order_release);
+    return e;
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+inline int num_sms() {
+    static std::atomic<int> n[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    const int slot = (dev >= 0 && dev < kMaxDevices) ? dev : 0;
+    int v = n[slot].load(std::memory_order_relaxed);
+    if (v <= 0) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        n[slot].store(v, std::memory_order_relaxed);
+    }
+    return v;
 }
 
 template <typename... KArgs, typename... Args>

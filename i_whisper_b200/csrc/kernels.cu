@@ -860,13 +860,9 @@ template <int QB, bool RING>
 static cudaError_t attention_cc_launch(const AttnArgs &a, int B, int H, cudaStream_t st) {
     const int tk_cap = a.Tk_cap > 0 ? a.Tk_cap : a.Tk;
     const size_t smem = (RING ? (size_t)kAttnRing * kAttnU * kAttnKeysPerPass * 64 : 0) + (size_t)QB * tk_cap * 3;
-    static size_t smem_set = 0;
-    if (smem > 48 * 1024 && smem > smem_set) {
-        cudaError_t e =
-            cudaFuncSetAttribute(attn_cc_kernel<QB, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_set = smem;
-    }
+    static SmemLimit lim;
+    cudaError_t e = raise_smem_limit(attn_cc_kernel<QB, RING>, smem, lim);
+    if (e != cudaSuccess) return e;
     dim3 grid((a.Tq + QB - 1) / QB, H, B);
     return launch_pdl(attn_cc_kernel<QB, RING>, grid, kAttnThreads, smem, st, a);
 }

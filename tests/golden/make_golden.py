@@ -18,6 +18,8 @@ of each block's INT15 stream, plus the greedy token ids). Needs the
 reference checkout and oracle/_ref (``make -C oracle ref``).
 
 Usage: python tests/golden/make_golden.py [REFERENCE_ROOT]
+(default: $IWHISPER_REFERENCE, else a checkout named ``reference`` next to
+this repository)
 """
 import hashlib
 import json
@@ -31,7 +33,10 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+sys.path.insert(0, HERE)
+from refroot import reference_root  # noqa: E402
+
+REF = None  # resolved on first use: argv[1], $IWHISPER_REFERENCE or ../reference
 
 from oracle import oracle as O  # noqa: E402
 from i_whisper_b200.checkpoint import ModelDims, synthetic_state_dict  # noqa: E402
@@ -91,7 +96,7 @@ def _bridge_C():
 def import_reference(ref: str = None, bridge=None):
     """Import the reference's model_int, modules.linear and decoding with
     ``_C`` served by ``bridge()`` (default: the reference scalar kernels)."""
-    ref = ref or REF
+    ref = ref or REF or reference_root(sys.argv[1] if __name__ == "__main__" and len(sys.argv) > 1 else None)
     for name in ("bitsandbytes", "bitsandbytes.functional", "matplotlib", "matplotlib.pyplot", "librosa"):
         sys.modules.setdefault(name, types.ModuleType(name))
     sys.modules["bitsandbytes"].functional = sys.modules["bitsandbytes.functional"]
@@ -108,10 +113,14 @@ def import_reference(ref: str = None, bridge=None):
     return MI, ML, DEC
 
 
-def run_reference(MI, ML, DEC, case, backend):
+def run_reference(MI, ML, DEC, case, backend, sd=None):
+    """The reference's Whisper_int encoder (with per-block digests) and its
+    DecodingTask greedy loop on ``backend``; ``sd`` defaults to the synthetic
+    checkpoint of ``case["seed"]``."""
     dims = case["dims"]
     model = MI.Whisper_int(MI.ModelDimensions(**dims.__dict__))
-    sd = synthetic_state_dict(dims, case["seed"])
+    if sd is None:
+        sd = synthetic_state_dict(dims, case["seed"])
     missing, unexpected = model.load_state_dict({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in sd.items()},
                                                 strict=True)
     assert not missing and not unexpected

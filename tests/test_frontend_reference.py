@@ -14,7 +14,9 @@ import torch
 from i_whisper_b200.frontend import mel_filterbank
 from i_whisper_b200.synthetic import log_mel, synthetic_audio
 
-REF = os.environ.get("IWHISPER_REFERENCE", "/root/reference")
+REF = os.environ.get("IWHISPER_REFERENCE",
+                     os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                                  "reference"))
 pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "i_whisper")), reason="no reference checkout")
 
 

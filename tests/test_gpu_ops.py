@@ -700,18 +700,19 @@ def test_linear8_headmajor(ops, L, B, T, N):
     assert np.array_equal(host(out), ref)
 
 
-@pytest.mark.parametrize("B,H,T", [(2, 6, 1500), (1, 16, 1500), (2, 8, 130), (3, 4, 64), (1, 6, 257)])
-@pytest.mark.parametrize("qk_s,fb", [(10, 7), (12, 7), (0, 7), (14, 9), (8, 5)])
-def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
-    """Encoder self-attention on the tcgen05 path (exp table + V^T) against
-    the oracle's three reference stages."""
+def _attention_tc_case(L, B, H, T, qk_m, qk_s, fb, seed, qkv_std=None):
+    """Encoder self-attention through iw_attention_ex on the tcgen05 path
+    (exp table + V^T) against the oracle's three reference stages."""
     import ctypes
     from i_whisper_b200 import _lib
-    rng = np.random.default_rng(B * 1000 + H * 10 + T + qk_s)
+    rng = np.random.default_rng(seed)
     d = H * 64
-    qkv = rng.integers(-127, 128, (B * T, 3 * d), dtype=np.int8)
+    if qkv_std is None:
+        qkv = rng.integers(-127, 128, (B * T, 3 * d), dtype=np.int8)
+    else:  # activations of a calibrated model: clipped normal
+        qkv = np.clip(np.rint(rng.normal(0, qkv_std, (B * T, 3 * d))), -127, 127).astype(np.int8)
     q = qkv[:, :d].reshape(B, T, d); k = qkv[:, d:2 * d].reshape(B, T, d); v = qkv[:, 2 * d:].reshape(B, T, d)
-    P = {"a.qk_req_multiplier": np.array([90], np.uint8), "a.qk_req_shiftmount": np.array([qk_s], np.int8),
+    P = {"a.qk_req_multiplier": np.array([qk_m], np.uint8), "a.qk_req_shiftmount": np.array([qk_s], np.int8),
          "a.qk_frac_bits": np.array(fb, np.int32), "a.av_req_multiplier": np.array([200], np.uint8),
          "a.av_req_shiftmount": np.array([8], np.int8)}
     ref = O.attention_core(L, P, "a", q, k, v, H, None)
@@ -729,7 +730,7 @@ def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
     a.v, a.ldv, a.v_bs, a.v_hs = base + 2 * d, 3 * d, T * 3 * d, 64
     a.y, a.ldy, a.y_bs, a.y_hs = out.data_ptr(), d, T * d, 64
     a.B, a.H, a.Tq, a.Tk = B, H, T, T
-    a.qk_multiplier, a.qk_shift, a.frac_bits = 90, qk_s, fb
+    a.qk_multiplier, a.qk_shift, a.frac_bits = qk_m, qk_s, fb
     a.av_multiplier, a.av_shift, a.rsqrt_offset = 200, 8, 16
     a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
     rsum = torch.full((B * T,), 7, dtype=torch.int32, device="cuda")  # added to, not overwritten
@@ -738,6 +739,37 @@ def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
     assert np.array_equal(host(out).reshape(B, T, d), ref)
     assert np.array_equal(host(rsum), ref.reshape(B * T, d).astype(np.int32).sum(1) + 7)
     assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("B,H,T", [(2, 6, 1500), (1, 16, 1500), (2, 8, 130), (3, 4, 64), (1, 6, 257)])
+@pytest.mark.parametrize("qk_s,fb", [(10, 7), (12, 7), (0, 7), (14, 9), (8, 5), (8, 13), (7, 14), (6, 15), (9, 16)])
+def test_attention_tensor_core(ops, L, B, H, T, qk_s, fb):
+    """The tcgen05 attention over shapes with query/key tails, for frac_bits
+    up to 16: the calibrated checkpoints use 13-15, whose shift-exp tables
+    reach 22796 (13, 14) and 32770 (15, 16) entries, and whose probabilities
+    exceed 127 for 15 and 16 (unsigned row sums)."""
+    _attention_tc_case(L, B, H, T, 90, qk_s, fb, B * 1000 + H * 10 + T + qk_s)
+
+
+@pytest.mark.parametrize("B,H,T", [(1, 6, 1500), (2, 4, 257)])
+@pytest.mark.parametrize("qk_m,qk_s", [(90, -3), (90, 1), (90, 31), (90, 32), (90, 40), (0, 8), (1, 8), (255, 8),
+                                       (255, 0), (1, 31)])
+@pytest.mark.parametrize("fb", [7, 14])
+def test_attention_tensor_core_requant_edges(ops, L, B, H, T, qk_m, qk_s, fb):
+    """The reference's score-requantisation edge cases on the tcgen05 path
+    (the general, non-fast kernel instance): negative shifts (no shift),
+    shift 31, shifts of 32 and more (every score 0), multipliers 0, 1 and
+    255 (qk_requant_rowmax_scalar, attention_scalar.cpp:216-343)."""
+    _attention_tc_case(L, B, H, T, qk_m, qk_s, fb, 77 + B + T + qk_m * 7 + (qk_s & 0xFF) * 131 + fb)
+
+
+@pytest.mark.parametrize("qk_m,qk_s,fb,std", [(118, 8, 13, 25.0), (70, 6, 14, 30.0), (64, 6, 15, 20.0),
+                                              (121, 7, 14, 40.0)])
+def test_attention_tensor_core_calibrated_ranges(ops, L, qk_m, qk_s, fb, std):
+    """Parameters and activation spreads as in the reference-calibrated
+    checkpoints (clipped-normal Q/K/V), where many more probabilities are
+    non-zero than with uniform inputs."""
+    _attention_tc_case(L, 2, 8, 1500, qk_m, qk_s, fb, 500 + qk_m + fb, qkv_std=std)
 
 
 @pytest.mark.parametrize("n_hist", [0, 1, 2, 3, 5])

@@ -46,3 +46,4 @@ def test_reference_kernel_suite_passes_on_the_mirror(tmp_path):
     unexpected = [n for n in failed if n.split("[")[0] not in EXPECTED_FAILURES]
     assert not unexpected, (unexpected, r.stdout[-3000:])
     assert len(passed) >= 1400, (len(passed), r.stdout[-2000:])
+

@@ -5,9 +5,12 @@ graphs with a pool they do not own, servers that pre-plan all device memory,
 foreign runtimes that only pass raw pointers) use iw_linear8_noalloc, which
 keeps the zero-point row sums in a fixed device array instead of a scratch
 allocation. This file checks, through the C ABI, that it returns exactly what
-iw_linear8 returns on two calls in a row (the shared array keeps the first
-call's contents when the second runs), and that sizes beyond its array are
-rejected. It is named so that pytest collects it after every other test.
+iw_linear8 returns on calls in a row -- a larger call first, then a smaller
+one that runs over the rows the first call left in the shared array, then
+one without a weight zero point -- that it takes nothing from the device's
+stream-ordered memory pool (where iw_linear8 takes its scratch), and that
+sizes beyond its array are rejected. It is named so that pytest collects it
+after every other test.
 """
 import ctypes
 
@@ -28,25 +31,73 @@ def _case(rng, M, K, N):
     return [torch.from_numpy(a).cuda() for a in (x, w, b, wz, m, s)]
 
 
-def _call(name, t, M, K, N):
+def _call(name, t, M, K, N, zero_point=True):
     from i_whisper_b200 import _lib
     x, w, b, wz, m, s = t
     y = torch.empty(M, N, dtype=torch.int8, device="cuda")
-    rc = getattr(_lib.LIB, name)(x.data_ptr(), w.data_ptr(), b.data_ptr(), wz.data_ptr(), m.data_ptr(), s.data_ptr(),
-                                 y.data_ptr(), M, K, N, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    rc = getattr(_lib.LIB, name)(x.data_ptr(), w.data_ptr(), b.data_ptr(), wz.data_ptr() if zero_point else None,
+                                 m.data_ptr(), s.data_ptr(), y.data_ptr(), M, K, N,
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc)
     return y
 
 
+class _PoolWatch:
+    """Used-memory high-water mark of the current device's stream-ordered
+    memory pool (the one cudaMallocAsync draws from), through the CUDA
+    runtime the library itself loads."""
+    USED_MEM_HIGH = 8  # cudaMemPoolAttrUsedMemHigh
+
+    def __init__(self):
+        self.rt = ctypes.CDLL("libcudart.so.12")
+        self.pool = ctypes.c_void_p()
+        assert self.rt.cudaDeviceGetMemPool(ctypes.byref(self.pool), torch.cuda.current_device()) == 0
+
+    def reset(self):
+        zero = ctypes.c_uint64(0)
+        assert self.rt.cudaMemPoolSetAttribute(self.pool, self.USED_MEM_HIGH, ctypes.byref(zero)) == 0
+
+    def high(self) -> int:
+        v = ctypes.c_uint64(0)
+        assert self.rt.cudaMemPoolGetAttribute(self.pool, self.USED_MEM_HIGH, ctypes.byref(v)) == 0
+        return v.value
+
+
 def test_noalloc_matches_linear8_twice():
     rng = np.random.default_rng(2024)
-    shapes = [(1500, 1024, 1024), (4096, 384, 1536)]  # second call: other M, K, N and inputs
+    # larger then smaller: the second call's rows are a prefix of what the
+    # first left in the shared array, so a read of stale rows would show
+    shapes = [(4096, 384, 1536), (1500, 1024, 1024)]
     for M, K, N in shapes:
         t = _case(rng, M, K, N)
         ref = _call("iw_linear8", t, M, K, N)
         got = _call("iw_linear8_noalloc", t, M, K, N)
         torch.cuda.synchronize()
         assert torch.equal(got, ref), (M, K, N)
+    # without a weight zero point the array is not used at all
+    M, K, N = 777, 512, 256
+    t = _case(rng, M, K, N)
+    ref = _call("iw_linear8", t, M, K, N, zero_point=False)
+    got = _call("iw_linear8_noalloc", t, M, K, N, zero_point=False)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+
+
+def test_noalloc_takes_nothing_from_the_memory_pool():
+    rng = np.random.default_rng(11)
+    M, K, N = 2000, 1024, 512
+    t = _case(rng, M, K, N)
+    _call("iw_linear8_noalloc", t, M, K, N)  # first call on this device: symbol lookup
+    torch.cuda.synchronize()
+    watch = _PoolWatch()
+    watch.reset()
+    _call("iw_linear8_noalloc", t, M, K, N)
+    torch.cuda.synchronize()
+    assert watch.high() == 0
+    # the check can see an allocation: iw_linear8 takes its row sums from the pool
+    _call("iw_linear8", t, M, K, N)
+    torch.cuda.synchronize()
+    assert watch.high() >= M * 4
 
 
 def test_noalloc_rejects_oversize_and_unpadded():
