@@ -63,8 +63,8 @@ def _i8(g: torch.Generator, *shape) -> torch.Tensor:
     return torch.randint(-127, 128, shape, dtype=torch.int8, generator=g).cuda()
 
 
-def _gauss_i8(g: torch.Generator, *shape) -> torch.Tensor:
-    return torch.clamp(torch.round(torch.randn(shape, generator=g) * 30.0), -127, 127).to(torch.int8).cuda()
+def _gauss_i8(g: torch.Generator, *shape, std: float = 30.0) -> torch.Tensor:
+    return torch.clamp(torch.round(torch.randn(shape, generator=g) * std), -127, 127).to(torch.int8).cuda()
 
 
 def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: int, gelu: str = "none",
@@ -154,24 +154,30 @@ def _attn_desc(q, ldq, q_bs, q_hs, k, ldk, k_bs, k_hs, v, ldv, v_bs, v_hs, y, ld
     return a
 
 
-def bench_attention(B: int, H: int, T: int, reps: int, seed: int) -> dict:
-    """Encoder self-attention straight from a fused QKV projection buffer."""
+def bench_attention(B: int, H: int, T: int, reps: int, seed: int, qk_m: int = 182, qk_s: int = 12, fb: int = 7,
+                    std: float = 30.0) -> dict:
+    """Encoder self-attention straight from a fused QKV projection buffer
+    (Q/K/V clipped normal with standard deviation ``std``; the score
+    requantisation and frac_bits of a layer: the calibrated whisper-medium
+    checkpoint has qk multipliers 64-126, shifts 6-8, frac_bits 13-14)."""
     g = torch.Generator().manual_seed(seed)
     d = H * 64
-    qkv = _gauss_i8(g, B * T, 3 * d)
+    qkv = _gauss_i8(g, B * T, 3 * d, std=std)
     out = torch.empty(B * T, d, dtype=torch.int8, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     tab = torch.empty(32772, dtype=torch.uint8, device="cuda")
-    _lib.call("iw_shift_exp_table", 7, tab.data_ptr(), stream)
+    _lib.call("iw_shift_exp_table", fb, tab.data_ptr(), stream)
     vt_ld = (T + 15) // 16 * 16
     vt = torch.empty(B * H * 64, vt_ld, dtype=torch.int8, device="cuda")
     base = qkv.data_ptr()
     a = _attn_desc(base, 3 * d, T * 3 * d, 64, base + d, 3 * d, T * 3 * d, 64, base + 2 * d, 3 * d, T * 3 * d, 64,
                    out.data_ptr(), d, T * d, B, H, T, T)
     a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
+    a.qk_multiplier, a.qk_shift, a.frac_bits = qk_m, qk_s, fb
     ms = _time(lambda: _lib.check(_lib.LIB.iw_attention_ex(C.byref(a), stream)), reps)
     tops = 4.0 * B * H * T * T * 64 / ms / 1e9
-    return {"op": "attention", "B": B, "H": H, "T": T, "ms": round(ms, 4), "tops": round(tops, 1),
+    return {"op": "attention", "B": B, "H": H, "T": T, "qk_multiplier": qk_m, "qk_shift": qk_s, "frac_bits": fb,
+            "std": std, "ms": round(ms, 4), "tops": round(tops, 1),
             "frac_of_datasheet_4500": round(tops / DATASHEET_INT8_TOPS, 4),
             "note": "ops count QK^T and P.V once (the kernel computes QK^T twice)"}
 
@@ -228,6 +234,10 @@ def main(argv=None):
     p.add_argument("--T", type=int, default=1500)
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--qk-mult", type=int, default=182, help="attention: qk requantisation multiplier")
+    p.add_argument("--qk-shift", type=int, default=12, help="attention: qk requantisation shift")
+    p.add_argument("--frac-bits", type=int, default=7, help="attention: shift-exp frac_bits")
+    p.add_argument("--std", type=float, default=30.0, help="attention: standard deviation of Q/K/V")
     a = p.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")
@@ -237,7 +247,7 @@ def main(argv=None):
     elif a.op == "layernorm":
         r = bench_layernorm(a.rows, a.d, a.reps, a.seed)
     elif a.op == "attention":
-        r = bench_attention(a.B, a.H, a.T, a.reps, a.seed)
+        r = bench_attention(a.B, a.H, a.T, a.reps, a.seed, a.qk_mult, a.qk_shift, a.frac_bits, a.std)
     elif a.op == "frontend":
         r = bench_frontend(a.B, a.n_mels, a.reps, a.seed)
     else:
