@@ -263,6 +263,14 @@ int iw_pv_norm_requant(const uint8_t *p, const int8_t *v, const int32_t *row_sum
                       "iw_pv_norm_requant");
 }
 
+// frac_bits of the fused attention entry points (the model's path). The
+// reference's _C.shift_exp wrapper admits [1, 14) (attention_torch.cpp:305;
+// iw_shift_exp keeps that check), but its own calibration writes 13-15 into
+// checkpoints, which the reference model runs on its torch backend; the
+// shift-exp arithmetic (1 << frac_bits in int32, attention_scalar.cpp:388-560)
+// is defined up to 30.
+static bool fused_frac_bits_ok(int32_t fb) { return fb >= 1 && fb <= 30; }
+
 int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, int64_t ldk, int64_t k_bs,
                  const int8_t *v, int64_t ldv, int64_t v_bs, int8_t *y, int64_t ldy, int64_t y_bs, int64_t B,
                  int64_t H, int64_t Tq, int64_t Tk, int mask_mode, const uint8_t *mask, uint8_t qk_multiplier,
@@ -271,7 +279,7 @@ int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, in
     if (B < 0 || H < 0 || Tq < 0 || Tk < 0) return fail(IW_EINVAL, "iw_attention: invalid shape");
     if (Tq > Tk && mask_mode == 1) return fail(IW_EINVAL, "iw_attention: causal mask needs Tq <= Tk");
     if (mask_mode == 2 && !mask) return fail(IW_EINVAL, "iw_attention: mask_mode 2 needs a mask");
-    if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    if (!fused_frac_bits_ok(frac_bits)) return fail(IW_EINVAL, "frac_bits must be in [1, 30]");
     if (!(rsqrt_offset >= 0 && rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
     if ((ldq | ldk | ldv | q_bs | k_bs | v_bs) & 15 ||
         (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
@@ -532,7 +540,7 @@ int iw_gelu_table(const uint8_t *lut, const uint8_t *luti_multiplier, const int8
 int iw_attention_ex(const iw_attn_desc *d, void *stream) {
     if (!d) return fail(IW_EINVAL, "iw_attention_ex: null descriptor");
     if (d->B < 0 || d->H < 0 || d->Tq < 0 || d->Tk < 0) return fail(IW_EINVAL, "iw_attention_ex: invalid shape");
-    if (!(d->frac_bits > 0 && d->frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    if (!fused_frac_bits_ok(d->frac_bits)) return fail(IW_EINVAL, "frac_bits must be in [1, 30]");
     if (!(d->rsqrt_offset >= 0 && d->rsqrt_offset <= 29)) return fail(IW_EINVAL, "rsqrt_offset must be in [0,29]");
     if (d->mask_mode == 2 && !d->mask) return fail(IW_EINVAL, "iw_attention_ex: mask_mode 2 needs a mask");
     if (((d->ldq | d->ldk | d->ldv | d->q_bs | d->k_bs | d->v_bs | d->q_hs | d->k_hs | d->v_hs) & 15) ||
@@ -563,7 +571,7 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream) {
 }
 
 int iw_shift_exp_table(int32_t frac_bits, uint8_t *table, void *stream) {
-    if (!(frac_bits > 0 && frac_bits < 14)) return fail(IW_EINVAL, "frac_bits must be in [1, 14)");
+    if (!fused_frac_bits_ok(frac_bits)) return fail(IW_EINVAL, "frac_bits must be in [1, 30]");
     cudaStream_t st = S(stream);
     Scratch sc(st);
     if (int r = cuda_check(sc.alloc(2 * sizeof(int)), "iw_shift_exp_table")) return r;

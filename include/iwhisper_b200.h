@@ -157,7 +157,9 @@ int iw_pv_norm_requant(const uint8_t *p, const int8_t *v, const int32_t *row_sum
  * mask_mode 0: none, 1: causal (key j masked when j > Tk-Tq+i, the slice of
  * TextDecoder_int.mask taken at model_int.py:786-799), 2: explicit mask
  * [Tq,Tk]. q, k, v and their row and batch strides must be multiples of
- * 16 bytes (IW_EINVAL otherwise). */
+ * 16 bytes (IW_EINVAL otherwise). frac_bits in [1, 30]: calibrated
+ * checkpoints carry up to 15, beyond the [1, 14) that the per-op
+ * iw_shift_exp admits like the reference's _C.shift_exp. */
 int iw_attention(const int8_t *q, int64_t ldq, int64_t q_bs, const int8_t *k, int64_t ldk, int64_t k_bs,
                  const int8_t *v, int64_t ldv, int64_t v_bs, int8_t *y, int64_t ldy, int64_t y_bs, int64_t B,
                  int64_t H, int64_t Tq, int64_t Tk, int mask_mode, const uint8_t *mask, uint8_t qk_multiplier,
@@ -338,8 +340,9 @@ int iw_attention_ex(const iw_attn_desc *d, void *stream);
 
 /* Shift-exp table (attention_scalar.cpp:388-560 as a function of the int16
  * difference to rowmax+1) for the tensor-core attention; table needs 32772
- * bytes. Synchronises `stream`; IW_EVALUE when frac_bits makes the table too
- * long for the tensor-core kernel (use the CUDA-core path then). */
+ * bytes (16-byte aligned for the kernel's vector copy into shared memory),
+ * frac_bits in [1, 30]. The whole table (at most 32770 entries, frac_bits >=
+ * 15) fits the kernel's shared memory. Synchronises `stream`. */
 int iw_shift_exp_table(int32_t frac_bits, uint8_t *table, void *stream);
 
 /* LayerNorm32 over rows with strides; optionally writes the row sums of the
