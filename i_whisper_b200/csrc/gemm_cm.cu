@@ -358,6 +358,28 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             const bool simple = __all_sync(
                 0xffffffffu, !cv || (ck.hmask == 0 && (MODE == EPI_L8 ? ck.q.sgn == -1 : ck.q.z == -1)));
 
+            // Linear32 + Residual15: the residuals of a chunk are loaded one
+            // chunk ahead (the first while the tile's MMAs run), so the epilogue
+            // does not wait a memory round trip per chunk. Each thread reads
+            // and writes only its own (row, channel) elements, so prefetching
+            // from the in-place residual is safe.
+            int32_t rv_next[kCmCh];
+            auto load_res = [&](int c) {
+                const int r0 = m0 + c * kCmCh;
+                const int16_t *res = p.res + (int64_t)r0 * p.ldr + n;
+                if (r0 + kCmCh <= Mt && p.ldr < (1 << 26)) {
+                    const uint32_t ldr32 = (uint32_t)p.ldr;
+#pragma unroll
+                    for (int j = 0; j < kCmCh; ++j) rv_next[j] = cv ? (int32_t)res[(uint32_t)j * ldr32] : 0;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kCmCh; ++j)
+                        rv_next[j] = (cv && r0 + j < Mt) ? (int32_t)res[(int64_t)j * p.ldr] : 0;
+                }
+            };
+            if constexpr (MODE == EPI_L32_RES) {
+                if (m0 + slice * kCmCh < Mt) load_res(slice);
+            }
             // every lane waits (the warp stays converged) for the bulk copies,
             // acquiring their data, and for the accumulator
             bool ok = mbar_wait(&aux_full[ab], aph) && mbar_wait(&tfull[buf], bphase);
@@ -419,20 +441,18 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                     }
                     if constexpr (MODE == EPI_L32_RES) {
                         // residual15_scalar.cpp:9-27 on the Linear32 output
+                        int32_t rv[kCmCh];
+#pragma unroll
+                        for (int j = 0; j < kCmCh; ++j) rv[j] = rv_next[j];
+                        const int cn = c + kCmEpiWarps / 4;  // this warp's next chunk
+                        if (cn < BR / kCmCh && m0 + cn * kCmCh < Mt) load_res(cn);
                         if (cv) {
                             const int rm = (int32_t)p.res_mult;
                             int16_t *out = reinterpret_cast<int16_t *>(p.out);
-                            // The residual is usually updated in place (res == out):
-                            // load the chunk's 32 residuals before the first store so
-                            // the loads overlap instead of waiting on each store.
-                            int32_t rv[kCmCh];
-                            const int16_t *res = p.res + (int64_t)r0 * p.ldr + n;
                             int16_t *o16 = out + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= Mt && p.ldr < (1 << 26) && p.ldo < (1 << 26)) {
+                            if (r0 + kCmCh <= Mt && p.ldo < (1 << 26)) {
                                 // whole chunk: 32-bit row offsets
-                                const uint32_t ldr32 = (uint32_t)p.ldr, ldo32 = (uint32_t)p.ldo;
-#pragma unroll
-                                for (int j = 0; j < kCmCh; ++j) rv[j] = res[(uint32_t)j * ldr32];
+                                const uint32_t ldo32 = (uint32_t)p.ldo;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
                                     int32_t t = u_mad(rv[j], rm, v[j]);
@@ -440,9 +460,6 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                     o16[(uint32_t)j * ldo32] = (int16_t)clampi(t, -16383, 16383);
                                 }
                             } else {
-#pragma unroll
-                                for (int j = 0; j < kCmCh; ++j)
-                                    rv[j] = (r0 + j < Mt) ? (int32_t)res[(int64_t)j * p.ldr] : 0;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
                                     if (r0 + j < Mt) {
