@@ -32,6 +32,14 @@ windows through the float log-mel frontend (seeds recycled modulo 32).
 * ``cpu_baseline``: the reference's own scalar C++ kernels (oracle/_ref) on a
   bounded sample of the same workload on the host cores (rank 0, N=1).
 
+``--config N`` selects another BASELINE configuration (default 3, the line
+above): 0 whisper-tiny, the seed-1 window, encoder + 32 greedy tokens; 1 the
+kernel microbench (w8a8 GEMM at M = 1500*{1,8,32} for four (K, N), integer
+LayerNorm over 1500 x 1024, 16-head 1500 x 1500 attention), each kernel
+timed per launch with an L2 flush in between; 2 whisper-small encoder, 32
+windows; 4 whisper-large encoder + 224 greedy tokens, 64 windows per GPU
+(512 over 8 GPUs).
+
 Multi-GPU: one process per GPU (torchrun); utterances are sharded by
 rank with no collective on the data path; ``scaling`` is weak (each rank
 owns a fixed batch). ``--impl reference`` times the reference CPU path
@@ -53,6 +61,28 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "int8 encoder 30s-windows/sec (whisper-medium) + % int8 TC peak; decoder tok/s"
+
+# model, windows per GPU, greedy tokens, window seeds
+CONFIGS = {
+    0: dict(model="tiny", batch=1, decode_tokens=32, seeds=[1],
+            workload="whisper-tiny integer encoder + 32 greedy tokens, batch 1, the seed-1 window (BASELINE configs[0])"),
+    1: dict(model="medium", batch=0, decode_tokens=0, seeds=None,
+            workload="kernel microbench (BASELINE configs[1]): w8a8 GEMM M=1500*{1,8,32} x (K,N) in "
+                     "{(1024,1024),(1024,4096),(4096,1024),(1280,5120)}, LayerNorm32 1500x1024, "
+                     "attention 16 heads x 1500^2 x 64"),
+    2: dict(model="small", batch=32, decode_tokens=0, seeds=None,
+            workload="whisper-small integer encoder, 32 windows per GPU (BASELINE configs[2])"),
+    3: dict(model="medium", batch=256, decode_tokens=128, seeds=None,
+            workload="whisper-medium integer encoder, {batch} windows per GPU (BASELINE configs[3]); "
+                     "greedy decoder {tokens} tokens"),
+    4: dict(model="large", batch=64, decode_tokens=224, seeds=None,
+            workload="whisper-large integer encoder, {batch} windows per GPU (512 over 8 GPUs, BASELINE "
+                     "configs[4]); greedy decoder {tokens} tokens"),
+}
+
+
+def metric_of(model: str) -> str:
+    return f"int8 encoder 30s-windows/sec (whisper-{model}) + % int8 TC peak; decoder tok/s"
 DATASHEET_INT8_TOPS = 4500.0
 ENC_GOP = {"tiny": 36.9, "small": 344.2, "medium": 1138.1, "large": 2273.8}
 
@@ -71,15 +101,23 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--model", default="medium")
-    ap.add_argument("--batch", type=int, default=256, help="windows per GPU")
-    ap.add_argument("--decode-tokens", type=int, default=128)
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS),
+                    help="BASELINE.json configuration (default 3: whisper-medium, 256 windows, 128 tokens)")
+    ap.add_argument("--model", default=None, help="override the configuration's model")
+    ap.add_argument("--batch", type=int, default=None, help="windows per GPU (override)")
+    ap.add_argument("--decode-tokens", type=int, default=None, help="greedy tokens (override)")
     ap.add_argument("--decode-runs", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-rows", type=int, default=64, help="query rows of the CPU sample")
     ap.add_argument("--phase", default="all", choices=["all", "encoder", "decoder"],
                     help="restrict the run (for profiling): encoder only, or decoder only")
-    return ap.parse_args()
+    a = ap.parse_args()
+    cfg = CONFIGS[a.config]
+    a.model = a.model or cfg["model"]
+    a.batch = cfg["batch"] if a.batch is None else a.batch
+    a.decode_tokens = cfg["decode_tokens"] if a.decode_tokens is None else a.decode_tokens
+    a.seeds = cfg["seeds"]
+    return a
 
 
 # ---------------------------------------------------------------------------
@@ -277,11 +315,14 @@ def load_golden(model: str, sd):
     if not os.path.exists(p):
         return None
     g = json.load(open(p))
-    key = {"medium": "medium_w2"}.get(model)
+    key = {"medium": "medium_w2", "tiny": "tiny_config0", "small": "small_w1", "large": "large_w1"}.get(model)
     ck = g.get("checkpoints", {}).get(model)
     if key not in g or not ck or ck["state_digest"] != state_digest(sd):
         return None
-    return g[key]
+    gold = dict(g[key])
+    if isinstance(gold["encoder_sha256"], str):  # a one-window fixture
+        gold["encoder_sha256"] = [gold["encoder_sha256"]]
+    return gold
 
 
 def check_parity(golden, xa, toks, seeds):
@@ -324,6 +365,8 @@ def main():
 
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.config == 1:
+        return micro_arm(args, rank, world)
 
     import torch
     import torch.distributed as dist
@@ -361,9 +404,10 @@ def main():
     model = WhisperIntB200(dims, sd)
     del sd
     start, stop = shard_bounds(B * world, world, rank)  # weak scaling: B utterances per rank
-    seeds = window_seeds(start, stop)
+    seeds = list(args.seeds) if args.seeds else window_seeds(start, stop)
     mels32 = synthetic_mel_batch(dims.n_mels, sorted(set(seeds)), input_alpha)
-    mel_np = np.stack([mels32[s % len(mels32)] for s in seeds])
+    by_seed = dict(zip(sorted(set(seeds)), mels32))
+    mel_np = np.stack([by_seed[s] for s in seeds])
     mel = torch.from_numpy(mel_np).cuda()
     enc_gops = enc_gop(dims)
 
@@ -413,7 +457,7 @@ def main():
     # ---- greedy decoder ------------------------------------------------------
     dec_tps = dec_e2e_tps = float("nan")
     dec_ms = float("nan")
-    if args.phase == "encoder":
+    if args.phase == "encoder" or args.decode_tokens <= 0:
         args.decode_runs = 0
     xa = model.encoder(mel)
     rs_xa = model._enc_ws[B]["rs_xa"]
@@ -475,7 +519,8 @@ def main():
     enc_tops = enc_gops * B * args.steps / (ms_per_step * args.steps * 1e-3) / 1e3
 
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": "windows/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric_of(args.model), "value": round(value, 3), "unit": "windows/s", "n_gpus": world,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": f"synthetic (seeded sine+noise windows; {weights})",
         "config": arm_config(args, world),
@@ -485,9 +530,9 @@ def main():
                              "of_datasheet_4500": round(enc_tops / DATASHEET_INT8_TOPS, 4)},
         "parity_checked": parity["all_ranks_ok"],
         "parity": parity,
-        "decoder": {"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
-                    "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
-                    "ms_per_decode": round(dec_ms / max(1, args.decode_runs), 2)},
+        "decoder": ({"tok_per_s": round(dec_tps, 1), "e2e_tok_per_s": round(dec_e2e_tps, 1),
+                     "tokens_per_utterance": args.decode_tokens, "utterances": B * world,
+                     "ms_per_decode": round(dec_ms / max(1, args.decode_runs), 2)} if args.decode_runs > 0 else None),
         "e2e": {"value": round(e2e_value, 3), "unit": "windows/s", "h2d_bytes_per_step": int(h_mel.numel()),
                 "d2h_bytes_per_step": int(h_out.numel())},
         "roofline": roof,
@@ -505,19 +550,125 @@ def main():
         dist.destroy_process_group()
 
 
+GEMM_SHAPES = [(1024, 1024), (1024, 4096), (4096, 1024), (1280, 5120)]
+
+
+def micro_arm(args, rank, world):
+    """BASELINE configs[1], the kernel microbench: every shape timed per
+    launch with CUDA events on its stream, a 256 MB write flushing L2 between
+    launches (most shapes fit in L2). One JSON line: ``value`` = the GEMMs'
+    aggregate TOPS over the twelve shapes; ``kernels`` = each kernel's rate
+    and roofline fraction. Rank 0 only (the shapes are single-GPU)."""
+    import torch
+    from i_whisper_b200 import microbench as MB, ops
+    if rank != 0:
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    cpu = None if args.no_cpu_baseline else cpu_kernel_baseline()
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    reps = max(1, args.steps)
+    launches = 0
+    kernels, g_ops, g_ms = [], 0.0, 0.0
+    with ClockSampler(local) as clk:
+        for Bw in (1, 8, 32):
+            for K, N in GEMM_SHAPES:
+                r = MB.bench_gemm(1500 * Bw, K, N, "linear8", 0, reps, 0, flush=flush, warmup=args.warmup)
+                g_ops += 2.0 * r["M"] * N * K * reps
+                g_ms += r["ms"] * reps
+                r["frac"] = round(r["tops"] / int8_peak, 4)
+                kernels.append(r)
+                launches += reps
+        ln = MB.bench_layernorm(1500, 1024, reps, 0, flush=flush, warmup=args.warmup)
+        # requantisation of the calibrated whisper-medium checkpoint's first layer
+        att = MB.bench_attention(1, 16, 1500, reps, 0, qk_m=68, qk_s=6, fb=14, std=30.0, flush=flush,
+                                 warmup=args.warmup)
+        att["frac"] = round(att["tops"] / int8_peak, 4)
+        kernels += [ln, att]
+        launches += 3 * reps  # LayerNorm, attention and its V^T transpose
+    tops = g_ops / (g_ms * 1e-3) / 1e12
+    # end to end through the public operator: host int8 x -> device -> linear8_cuda -> host
+    M, K, N = 48000, 1024, 1024
+    g = torch.Generator().manual_seed(0)
+    hx = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g).pin_memory()
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g).cuda()
+    mult = torch.full((N,), 1 << 30, dtype=torch.uint32, device="cuda")
+    shift = torch.full((N,), 20, dtype=torch.int8, device="cuda")
+    hy = torch.empty(M, N, dtype=torch.int8).pin_memory()
+    for _ in range(args.warmup):
+        hy.copy_(ops.linear8_cuda(hx.cuda(non_blocking=True), w, None, None, mult, shift), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        hy.copy_(ops.linear8_cuda(hx.cuda(non_blocking=True), w, None, None, mult, shift), non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e2e = 2.0 * M * N * K * reps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    line = {"metric": "int8 kernel microbench: w8a8 GEMM TOPS over 12 shapes (+ LayerNorm GB/s, attention TOPS)",
+            "value": round(tops, 1), "unit": "TOPS", "n_gpus": 1, "steps": reps, "warmup": args.warmup,
+            "ms_per_step": round(g_ms / reps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded uniform INT8, per-channel frexp scales, N(0,30) Q/K/V)",
+            "config": {"workload": CONFIGS[1]["workload"], "baseline_config": 1, "model": "kernels",
+                       "global_batch": 1, "seq_len": 1500, "parallelism": "single GPU",
+                       "l2": "flushed between launches (256 MB write)"},
+            "roofline": {"kernel": "gemm_i8 (12 shapes)", "bound": "tensor", "achieved": round(tops, 1),
+                         "peak": round(int8_peak, 1), "unit": "TFLOP/s", "frac": round(tops / int8_peak, 4),
+                         "peak_source": "2 x MEASURED_PEAKS.json bf16_tflops" + (" [fallback]" if peaks.get("fallback") else ""),
+                         "frac_of_datasheet_4500": round(tops / DATASHEET_INT8_TOPS, 4), "traffic": None},
+            "kernels": kernels,
+            "e2e": {"value": round(e2e, 1), "unit": "TOPS", "h2d_bytes_per_step": M * K, "d2h_bytes_per_step": M * N,
+                    "note": "ops.linear8_cuda M=48000 K=N=1024 with the host input copied in and the output read back"},
+            "gpu_launches": int(launches), "clocks": clk.summary()}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def cpu_kernel_baseline():
+    """The reference's own scalar linear8 (oracle/_ref, or the port) on one
+    host core over the smallest microbench GEMM (M=1500, K=N=1024)."""
+    from oracle import oracle as O
+    kind = "reference" if os.path.exists(O.REF_PATH) else "port"
+    L = O.lib("ref" if kind == "reference" else "port")
+    if kind == "port":
+        L.set_threads(1)
+    rng = np.random.default_rng(0)
+    M, K, N = 1500, 1024, 1024
+    x = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    m = np.full(N, 1 << 30, np.uint32)
+    sh = np.full(N, 20, np.int8)
+    t0 = time.perf_counter()
+    L.linear8(x, w, None, None, m, sh)
+    dt = time.perf_counter() - t0
+    return {"value": round(2.0 * M * N * K / dt / 1e12, 6), "unit": "TOPS", "cores": 1, "kind": kind,
+            "sample": "one linear8 of M=1500, K=N=1024 on one host core"}
+
+
 def arm_config(args, world):
     """The workload both arms report (the reference arm times a bounded sample
     of it on the host cores, see its cpu_baseline.sample)."""
-    return {"workload": f"whisper-{args.model} integer encoder, {args.batch} windows per GPU (BASELINE configs[3]); "
-                        f"greedy decoder {args.decode_tokens} tokens",
+    cfg = CONFIGS[args.config]
+    work = cfg["workload"].format(batch=args.batch, tokens=args.decode_tokens)
+    if (args.model, args.batch, args.decode_tokens) != (cfg["model"], cfg["batch"], cfg["decode_tokens"]):
+        work = (f"whisper-{args.model} integer encoder, {args.batch} windows per GPU; greedy decoder "
+                f"{args.decode_tokens} tokens (overrides of BASELINE configs[{args.config}])")
+    big = args.batch * 1500 * 1024 > 126e6
+    return {"workload": work, "baseline_config": args.config,
             "model": f"whisper-{args.model}", "global_batch": args.batch * world, "seq_len": 1500,
             "parallelism": f"utterance-sharded x{world}",
-            "l2": "working set per step > 5 GB (inputs larger than L2)"}
+            "l2": ("working set per step > 5 GB (inputs larger than L2)" if big else
+                   "working set per step below L2 (126 MB): timed as resident, no flush")}
 
 
 def reference_arm(args, rank, world):
     if rank != 0:
         return
+    if args.config == 1:
+        return reference_micro_arm(args, world)
     procs = os.cpu_count() or 1
     vals = []
     for _ in range(args.warmup):
@@ -529,7 +680,8 @@ def reference_arm(args, rank, world):
     cw = float(np.mean([v[0] for v in vals]))
     ct = float(np.mean([v[1] for v in vals]))
     kind, cores, sample = vals[0][2], vals[0][3], vals[0][4]
-    line = {"impl": "reference", "metric": METRIC, "value": round(cw, 6), "unit": "windows/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": metric_of(args.model), "value": round(cw, 6), "unit": "windows/s",
+            "n_gpus": world,
             # ms_per_step is the timed sample step on the host; the metric is
             # extrapolated from it to whole windows (cpu_baseline.sample)
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / args.steps, 1),
@@ -541,6 +693,26 @@ def reference_arm(args, rank, world):
                              "sample": sample},
             "e2e": {"value": round(cw, 6), "unit": "windows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": round(wall, 1)}
+    print(json.dumps(line), flush=True)
+
+
+def reference_micro_arm(args, world):
+    """The reference arm of the kernel microbench: the reference's scalar
+    linear8 on one host core, one bounded sample per step."""
+    for _ in range(args.warmup):
+        cpu_kernel_baseline()
+    t0 = time.time()
+    vals = [cpu_kernel_baseline() for _ in range(args.steps)]
+    wall = time.time() - t0
+    v = float(np.mean([c["value"] for c in vals]))
+    cb = dict(vals[0], value=round(v, 6))
+    line = {"impl": "reference", "metric": "int8 kernel microbench: w8a8 GEMM TOPS over 12 shapes (+ LayerNorm GB/s, "
+            "attention TOPS)", "value": round(v, 6), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(wall * 1e3 / max(1, args.steps), 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": CONFIGS[1]["workload"], "baseline_config": 1, "model": "kernels"},
+            "cpu_baseline": cb, "e2e": {"value": round(v, 6), "unit": "TOPS", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 

@@ -45,18 +45,31 @@ def hbm_peak():
         return 6650.0, "fallback"
 
 
-def _time(fn, reps: int, warmup: int = 3) -> float:
+def _time(fn, reps: int, warmup: int = 3, flush: torch.Tensor = None) -> float:
+    """Mean ms per launch of fn on the current stream (CUDA events). With
+    ``flush`` (a buffer larger than L2) each launch is timed alone, after a
+    write of the buffer that evicts L2, so the inputs come from HBM."""
     for _ in range(warmup):
         fn()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    e0.record(st)
+    if flush is None:
+        e0.record(st)
+        for _ in range(reps):
+            fn()
+        e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+    total = 0.0
     for _ in range(reps):
+        flush.fill_(1)
+        e0.record(st)
         fn()
-    e1.record(st)
-    e1.synchronize()
-    return e0.elapsed_time(e1) / reps
+        e1.record(st)
+        e1.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / reps
 
 
 def _i8(g: torch.Generator, *shape) -> torch.Tensor:
@@ -68,7 +81,7 @@ def _gauss_i8(g: torch.Generator, *shape, std: float = 30.0) -> torch.Tensor:
 
 
 def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: int, gelu: str = "none",
-               rowsum_out: bool = False) -> dict:
+               rowsum_out: bool = False, flush: torch.Tensor = None, warmup: int = 3) -> dict:
     g = torch.Generator().manual_seed(seed)
     x, w = _i8(g, M, K), _i8(g, N, K)
     rng = np.random.default_rng(seed)
@@ -119,7 +132,7 @@ def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: 
         d.residual, d.ldr, d.residual_multiplier = res.data_ptr(), N, 23000
         out_bytes = 4 * M * N
     d.out, d.ldo = out.data_ptr(), N
-    ms = _time(lambda: _lib.check(_lib.LIB.iw_gemm_i8(C.byref(d), stream)), reps)
+    ms = _time(lambda: _lib.check(_lib.LIB.iw_gemm_i8(C.byref(d), stream)), reps, warmup, flush)
     tops = 2.0 * M * N * K / ms / 1e9
     return {"op": "gemm", "mode": mode, "gelu": gelu, "rowsum_out": rowsum_out, "M": M, "K": K, "N": N,
             "tile_n": tile_n, "ms": round(ms, 4),
@@ -127,7 +140,7 @@ def bench_gemm(M: int, K: int, N: int, mode: str, tile_n: int, reps: int, seed: 
             "algorithmic_bytes": M * K + N * K + out_bytes}
 
 
-def bench_layernorm(rows: int, d: int, reps: int, seed: int) -> dict:
+def bench_layernorm(rows: int, d: int, reps: int, seed: int, flush: torch.Tensor = None, warmup: int = 3) -> dict:
     g = torch.Generator().manual_seed(seed)
     x = torch.randint(-16383, 16384, (rows, d), dtype=torch.int16, generator=g).cuda()
     gamma = _i8(g, d)
@@ -135,7 +148,7 @@ def bench_layernorm(rows: int, d: int, reps: int, seed: int) -> dict:
     y = torch.empty(rows, d, dtype=torch.int8, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     ms = _time(lambda: _lib.call("iw_layernorm32", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), 180, 9,
-                                 1 << 30, 18, y.data_ptr(), rows, d, stream), reps)
+                                 1 << 30, 18, y.data_ptr(), rows, d, stream), reps, warmup, flush)
     hbm, src = hbm_peak()
     gbs = rows * d * 3 / ms / 1e6
     return {"op": "layernorm32", "rows": rows, "d": d, "ms": round(ms, 4), "gbs": round(gbs, 1),
@@ -155,7 +168,7 @@ def _attn_desc(q, ldq, q_bs, q_hs, k, ldk, k_bs, k_hs, v, ldv, v_bs, v_hs, y, ld
 
 
 def bench_attention(B: int, H: int, T: int, reps: int, seed: int, qk_m: int = 182, qk_s: int = 12, fb: int = 7,
-                    std: float = 30.0) -> dict:
+                    std: float = 30.0, flush: torch.Tensor = None, warmup: int = 3) -> dict:
     """Encoder self-attention straight from a fused QKV projection buffer
     (Q/K/V clipped normal with standard deviation ``std``; the score
     requantisation and frac_bits of a layer: the calibrated whisper-medium
@@ -174,7 +187,7 @@ def bench_attention(B: int, H: int, T: int, reps: int, seed: int, qk_m: int = 18
                    out.data_ptr(), d, T * d, B, H, T, T)
     a.exp_table, a.vt, a.vt_ld = tab.data_ptr(), vt.data_ptr(), vt_ld
     a.qk_multiplier, a.qk_shift, a.frac_bits = qk_m, qk_s, fb
-    ms = _time(lambda: _lib.check(_lib.LIB.iw_attention_ex(C.byref(a), stream)), reps)
+    ms = _time(lambda: _lib.check(_lib.LIB.iw_attention_ex(C.byref(a), stream)), reps, warmup, flush)
     tops = 4.0 * B * H * T * T * 64 / ms / 1e9
     return {"op": "attention", "B": B, "H": H, "T": T, "qk_multiplier": qk_m, "qk_shift": qk_s, "frac_bits": fb,
             "std": std, "ms": round(ms, 4), "tops": round(tops, 1),

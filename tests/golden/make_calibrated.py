@@ -35,6 +35,9 @@ content digests are recorded so a test can tell it has the same weights):
   and 8 greedy tokens, computed by the oracle (oracle/, the C restatement
   pinned to the reference kernels), plus, for window 0, the encoder output
   digest of the reference's own graph on its ``torch`` backend.
+* ``small_w1``, ``large_w1``: the calibrated whisper-small and whisper-large
+  models on the window seeded 0: encoder output digest and 8 greedy tokens
+  from the oracle.
 
 Usage: python tests/golden/make_calibrated.py [--reference PATH] [--sizes tiny,medium]
        [--ckpt DIR] [--skip-golden]
@@ -166,6 +169,24 @@ def golden_medium(sd, seeds=(0, 1), sample_len=8):
     return out
 
 
+def golden_oracle(size, sd, seeds=(0,), sample_len=8):
+    """Oracle digests of the calibrated ``size`` model on windows ``seeds``:
+    encoder output per window and ``sample_len`` greedy tokens."""
+    from oracle import oracle as O
+    from i_whisper_b200.model import decode_tokens
+    dims = DIMS[size]
+    mel = synthetic_mel_batch(dims.n_mels, list(seeds), float(sd["encoder.input_alpha"][0]))
+    t0 = time.time()
+    xa = O.encoder_forward(sd, O.Dims(**dims.__dict__), mel)
+    t = decode_tokens(dims.n_vocab)
+    spec = O.DecodeTokens(sot=t["sot"], eot=t["eot"], sot_sequence=t["sot_sequence"], no_timestamps=t["no_timestamps"],
+                          timestamp_begin=t["timestamp_begin"], blank=t["blank"], suppress=t["suppress"])
+    toks = O.greedy_decode(sd, O.Dims(**dims.__dict__), xa, spec, sample_len, stop_when_done=False)
+    print(f"  {size} oracle: {time.time() - t0:.1f} s, tokens {toks.tolist()}")
+    return dict(dims=dims.__dict__, mel_seeds=list(seeds), sample_len=sample_len, source="oracle (C restatement)",
+                mel_sha256=[sha(m) for m in mel], encoder_sha256=[sha(x) for x in xa], tokens=toks.tolist())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=None)
@@ -201,6 +222,8 @@ def main():
             golden["tiny_config0"] = golden_tiny(sd)
         elif size == "medium":
             golden["medium_w2"] = golden_medium(sd)
+        else:
+            golden[f"{size}_w1"] = golden_oracle(size, sd)
     with open(GOLDEN, "w") as f:
         json.dump(golden, f, indent=1)
 

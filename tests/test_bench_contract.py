@@ -55,3 +55,20 @@ def test_encoder_work_formula_matches_the_published_table():
     from i_whisper_b200.checkpoint import DIMS
     for name, gop in bench.ENC_GOP.items():
         assert round(bench.enc_gop(DIMS[name]), 1) == gop, name
+
+
+def test_reference_arm_follows_the_config():
+    """--config selects BASELINE configurations: 0 is whisper-tiny on one
+    window, 1 the kernel microbench (the reference's linear8 in TOPS)."""
+    r0 = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "0", "--steps", "1",
+                         "--warmup", "0", "--cpu-rows", "16"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r0.returncode == 0, r0.stderr[-2000:]
+    d0 = json.loads([ln for ln in r0.stdout.splitlines() if ln.startswith("{")][0])
+    assert d0["config"]["baseline_config"] == 0 and "whisper-tiny" in d0["config"]["workload"]
+    assert "whisper-tiny" in d0["metric"]
+    r1 = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "1", "--steps", "1",
+                         "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r1.returncode == 0, r1.stderr[-2000:]
+    d1 = json.loads([ln for ln in r1.stdout.splitlines() if ln.startswith("{")][0])
+    assert d1["unit"] == "TOPS" and d1["value"] > 0 and d1["config"]["baseline_config"] == 1
+    assert d1["cpu_baseline"]["cores"] == 1 and d1["e2e"]["unit"] == "TOPS"
