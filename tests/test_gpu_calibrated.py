@@ -123,3 +123,18 @@ def test_medium_batch256_matches_oracle_and_batch1():
     assert np.array_equal(x1.cpu().numpy()[0], xa_h[255])
     assert t1.cpu().numpy()[0].tolist() == toks_h[255].tolist()
     assert _lib.device_status(clear=True) == 0
+
+
+def test_graphed_encoder_equals_eager():
+    """encoder_graphed (one CUDA graph per batch size) gives the eager
+    encoder's bytes, on two calls in a row with different inputs."""
+    from i_whisper_b200 import _lib
+    model, sd, g = calibrated_model("tiny")
+    alpha = float(sd["encoder.input_alpha"][0])
+    for seeds in ([3, 4], [5, 6]):
+        mel = torch.from_numpy(synthetic_mel_batch(80, seeds, alpha)).cuda()
+        ref = model.encoder(mel).clone()
+        got = model.encoder_graphed(mel)
+        assert torch.equal(got, ref), seeds
+    assert model.graph_launches[("encoder", 2)] > 0
+    assert _lib.device_status(clear=True) == 0
