@@ -594,6 +594,11 @@ def micro_arm(args, rank, world):
                 kernels.append(r)
                 launches += reps
         ln = MB.bench_layernorm(1500, 1024, reps, 0, flush=flush, warmup=args.warmup)
+        # the same kernel at the encoder's size in configuration 3 (256 windows x 1500 rows)
+        ln_enc = MB.bench_layernorm(1500 * 256, 1024, reps, 0, flush=flush, warmup=args.warmup)
+        ln_enc["note"] = "the encoder's LayerNorm at 256 windows (configuration 3's batch)"
+        kernels.append(ln_enc)
+        launches += reps
         # requantisation of the calibrated whisper-medium checkpoint's first layer
         att = MB.bench_attention(1, 16, 1500, reps, 0, qk_m=68, qk_s=6, fb=14, std=30.0, flush=flush,
                                  warmup=args.warmup)

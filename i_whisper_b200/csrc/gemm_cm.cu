@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
     // Measured on the GeLU-table path (fc1: 1739 vs 1650 TOPS); the plain
     // Linear8 epilogue keeps single-byte stores (QKV: 1939 vs 1878 TOPS).
     const bool quad_rows = MODE == EPI_L8 && GT && !p.posadd && (N & 3) == 0 && (p.ldo & 3) == 0 &&
-                           p.ldo < (1 << 27) && (reinterpret_cast<uintptr_t>(p.out) & 3) == 0;
+                           (reinterpret_cast<uintptr_t>(p.out) & 3) == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -367,10 +367,15 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             auto load_res = [&](int c) {
                 const int r0 = m0 + c * kCmCh;
                 const int16_t *res = p.res + (int64_t)r0 * p.ldr + n;
-                if (r0 + kCmCh <= Mt && p.ldr < (1 << 26)) {
-                    const uint32_t ldr32 = (uint32_t)p.ldr;
+                if (r0 + kCmCh <= Mt) {
+                    // one pointer stepped by the row stride: measured cheaper
+                    // than a 32-bit row offset per element (j * ld) added to
+                    // a 64-bit base
 #pragma unroll
-                    for (int j = 0; j < kCmCh; ++j) rv_next[j] = cv ? (int32_t)res[(uint32_t)j * ldr32] : 0;
+                    for (int j = 0; j < kCmCh; ++j) {
+                        rv_next[j] = cv ? (int32_t)*res : 0;
+                        res += p.ldr;
+                    }
                 } else {
 #pragma unroll
                     for (int j = 0; j < kCmCh; ++j)
@@ -450,14 +455,14 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             const int rm = (int32_t)p.res_mult;
                             int16_t *out = reinterpret_cast<int16_t *>(p.out);
                             int16_t *o16 = out + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= Mt && p.ldo < (1 << 26)) {
-                                // whole chunk: 32-bit row offsets
-                                const uint32_t ldo32 = (uint32_t)p.ldo;
+                            if (r0 + kCmCh <= Mt) {
+                                // whole chunk: the row pointer stepped by the stride
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {
                                     int32_t t = u_mad(rv[j], rm, v[j]);
                                     t = u_add(u_add(t, 1 << 14), t >> 31) >> 15;
-                                    o16[(uint32_t)j * ldo32] = (int16_t)clampi(t, -16383, 16383);
+                                    *o16 = (int16_t)clampi(t, -16383, 16383);
+                                    o16 += p.ldo;
                                 }
                             } else {
 #pragma unroll
@@ -508,16 +513,20 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                 int b = r0 / p.tr_T, t = r0 - (r0 / p.tr_T) * p.tr_T;
                                 const bool vec = (p.tr_T & 3) == 0 && (p.tr_ld & 3) == 0 &&
                                                  (reinterpret_cast<uintptr_t>(p.tr_out) & 3) == 0;
+                                // (with tr_T % 4 == 0 and r0 % 16 == 0 a group of four
+                                // rows never straddles two batches; dst follows (b, t))
+                                int8_t *dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
+                                const int64_t bstep = (int64_t)p.tr_N * p.tr_ld - p.tr_T;
 #pragma unroll
                                 for (int j = 0; j < kCmCh; j += 4) {
                                     const int m = r0 + j;
                                     if (vec && m + 3 < Mt) {
-                                        int8_t *dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
                                         *reinterpret_cast<uint32_t *>(dst) =
                                             (uint32_t)(uint8_t)v[j] | ((uint32_t)(uint8_t)v[j + 1] << 8) |
                                             ((uint32_t)(uint8_t)v[j + 2] << 16) | ((uint32_t)(uint8_t)v[j + 3] << 24);
                                         t += 4;
-                                        if (t == p.tr_T) { t = 0; ++b; }
+                                        dst += 4;
+                                        if (t == p.tr_T) { t = 0; ++b; dst += bstep; }
                                     } else {
 #pragma unroll
                                         for (int u = 0; u < 4; ++u) {
@@ -526,6 +535,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                                     (int8_t)v[j + u];
                                             if (++t == p.tr_T) { t = 0; ++b; }
                                         }
+                                        dst = p.tr_out + ((int64_t)b * p.tr_N + (n - p.tr_c0)) * p.tr_ld + t;
                                     }
                                 }
                             }
@@ -560,22 +570,25 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                             const uint32_t sel2 = (gi & 1) ? 0x3715u : 0x6240u;
                             const int cn = n0 + quad * 32 + (lane & ~3);
                             int8_t *ob = reinterpret_cast<int8_t *>(p.out) + (int64_t)(r0 + gi) * p.ldo + cn;
-                            const uint32_t ldo32 = (uint32_t)p.ldo;
+                            const int64_t ld4 = 4 * p.ldo;
 #pragma unroll
                             for (int q = 0; q < kCmCh / 4; ++q) {
                                 const uint32_t w = __byte_perm(__byte_perm(v[4 * q], v[4 * q + 1], 0x0040u),
                                                                __byte_perm(v[4 * q + 2], v[4 * q + 3], 0x0040u), 0x5410u);
                                 const uint32_t x = __byte_perm(w, __shfl_xor_sync(0xffffffffu, w, 2), sel1);
                                 const uint32_t t = __byte_perm(x, __shfl_xor_sync(0xffffffffu, x, 1), sel2);
-                                if (cn < N) *reinterpret_cast<uint32_t *>(ob + (uint32_t)(4 * q) * ldo32) = t;
+                                if (cn < N) *reinterpret_cast<uint32_t *>(ob) = t;
+                                ob += ld4;
                             }
                         } else if (cv) {
                             int8_t *out = reinterpret_cast<int8_t *>(p.out) + (int64_t)r0 * p.ldo + n;
-                            if (r0 + kCmCh <= Mt && p.ldo < (1 << 27)) {
-                                // 32-bit row offsets: one wide multiply-add per address
-                                const uint32_t ldo32 = (uint32_t)p.ldo;
+                            if (r0 + kCmCh <= Mt) {
+                                // whole chunk: the row pointer stepped by the stride
 #pragma unroll
-                                for (int j = 0; j < kCmCh; ++j) out[(uint32_t)j * ldo32] = (int8_t)v[j];
+                                for (int j = 0; j < kCmCh; ++j) {
+                                    *out = (int8_t)v[j];
+                                    out += p.ldo;
+                                }
                             } else {
 #pragma unroll
                                 for (int j = 0; j < kCmCh; ++j) {

@@ -121,6 +121,25 @@ def test_layernorm32(ops, L, d, rows):
         assert np.array_equal(host(b), a)
 
 
+@pytest.mark.parametrize("d", [384, 1024, 1280])
+def test_layernorm32_rows_beyond_one_wave(ops, L, d):
+    """More rows than resident warps: each warp strides over several rows,
+    prefetching the next while it normalises the current one; the row count
+    leaves a ragged last stride. (The model's row-sum outputs are covered at
+    384000 rows by the calibrated batch-256 test.)"""
+    rng = np.random.default_rng(d)
+    rows = 40009
+    x = rng.integers(-16383, 16384, (rows, d), dtype=np.int16)
+    x[::97] //= 64
+    g = rng.integers(-127, 128, d, dtype=np.int8)
+    be = rng.integers(-(2 ** 20), 2 ** 20, d, dtype=np.int32)
+    ref = L.layernorm32(x, g, be, 200, 5, 2 ** 31 + 12345, 7)
+    got = ops.layernorm32_cuda(dev(x), dev(g), dev(be), torch.tensor([200], dtype=torch.uint8),
+                               torch.tensor([5], dtype=torch.int8), torch.tensor([2 ** 31 + 12345], dtype=torch.uint32),
+                               torch.tensor([7], dtype=torch.int8))
+    assert np.array_equal(host(got), ref)
+
+
 @pytest.mark.parametrize("d", [384, 768, 1280])
 def test_layernorm32_full_range(ops, L, d):
     """Rows beyond INT15, where the reference's int32 centred squares wrap."""
