@@ -32,6 +32,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "iw_common.cuh"
 #include "iw_sm100.cuh"
@@ -370,21 +371,41 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         uint32_t cidx = 0;
         const uint32_t negm = 0u - p.qk_mult;
         // exp of 32 scores of one half into eight packed words, adding to rs
+        // fast-path exp of 32 scores into eight packed words; MASKED: keep
+        // only the first `valid` (1..31) keys. Keys past T (a ragged last
+        // block) hold the scores of whatever K rows follow (the next window's,
+        // or the zero fill past the tensor): their index is clamped to the
+        // table like any other and their bytes are masked off afterwards.
+        // valid is the same for every lane, so the masks are warp-uniform.
+        auto exp_fast = [&](const uint32_t (&a)[32], int valid, uint32_t (&w4)[8], int32_t &rs, auto masked) {
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+                uint32_t ww = 0;
+#pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4) {
+                    const uint32_t idx = min(exp_index(a[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
+                    // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
+                    asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
+                }
+                if constexpr (decltype(masked)::value) {
+                    const int left = valid - 4 * q4;  // valid keys among this word's four
+                    ww &= left >= 4 ? 0xFFFFFFFFu : (left <= 0 ? 0u : (1u << (8 * left)) - 1u);
+                }
+                // probabilities are unsigned bytes (up to 255 for frac_bits >= 15)
+                rs = (int32_t)__dp4a(ww, 0x01010101u, (uint32_t)rs);
+                w4[q4] = ww;
+            }
+        };
+        // exp of 32 scores of one half into eight packed words, adding to rs
         auto exp_half = [&](const uint32_t (&a)[32], int valid, uint32_t (&w4)[8], int32_t &rs) {
             if (FAST && warp_simple && valid >= 32) {
+                exp_fast(a, valid, w4, rs, std::false_type{});
+            } else if (valid <= 0) {
+                // keys past T only (warp-uniform): probabilities 0
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
-                    uint32_t ww = 0;
-#pragma unroll
-                    for (int k4 = 0; k4 < 4; ++k4) {
-                        const uint32_t idx = min(exp_index(a[q4 * 4 + k4], negm, cidx) >> p.qk_sh, t1);
-                        // ww += tab << 8*k4 as a multiply-add (keeps it off the ALU pipe)
-                        asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(ww) : "r"((uint32_t)sTab[idx]), "r"(1u << (8 * k4)));
-                    }
-                    // probabilities are unsigned bytes (up to 255 for frac_bits >= 15)
-                    rs = (int32_t)__dp4a(ww, 0x01010101u, (uint32_t)rs);
-                    w4[q4] = ww;
-                }
+                for (int q4 = 0; q4 < 8; ++q4) w4[q4] = 0;
+            } else if (FAST && warp_simple) {
+                exp_fast(a, valid, w4, rs, std::true_type{});
             } else {
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
