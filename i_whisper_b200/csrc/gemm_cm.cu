@@ -128,8 +128,9 @@ IW_DEV int32_t gelu_tab_k(int32_t x, const uint8_t *gb) { return (int32_t)gb[x *
 // (ALU), 2 from the per-channel lookup table.
 template <int BR, int MODE, int GK>
 __global__ void __launch_bounds__(kCmThreads, 1)
-    gemm_cm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N,
-                   int K, int WR, const EpiParams p) {
+    gemm_cm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   const __grid_constant__ CUtensorMap tmR, int M, int N, int K, int WR, const EpiParams p,
+                   bool res_prefetch) {
     using Cfg = CmCfg<BR, GK>;
     constexpr int S = Cfg::STAGES;
     constexpr bool GT = GK == 2;
@@ -202,6 +203,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
         fence_mbar_init();
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmX);
+        if (MODE == EPI_L32_RES && res_prefetch) prefetch_tmap(&tmR);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -241,6 +243,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                     aux_parity = (aux_parity & ~(1u << ab)) | (aph << ab);
                     if (++ab == 2) { ab = 0; aph ^= 1; }
                 }
+                // Linear32 + Residual15: the tile's residual block (BR rows x
+                // 128 int16 channels) into L2 now, so that the epilogue's
+                // residual loads, a main loop later, hit L2
+                if (MODE == EPI_L32_RES && res_prefetch) tma_prefetch_l2_2d(&tmR, n0 * 2, m0);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
@@ -669,6 +675,13 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
     else
         e = make_tmap_2d_u8(&tx, g.x, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.ldx, kBlockK, BR);
     if (e != cudaSuccess) return e;
+    // residual block prefetch map (bytes: 128 int16 channels x BR rows); off
+    // when the residual is not 16-byte aligned for the tensor map
+    CUtensorMap tr = tx;
+    bool res_pf = false;
+    if (MODE == EPI_L32_RES && p.res && (reinterpret_cast<uintptr_t>(p.res) & 15) == 0 && ((p.ldr * 2) & 15) == 0)
+        res_pf = make_tmap_2d_u8(&tr, p.res, (uint64_t)g.N * 2, (uint64_t)g.M, (uint64_t)p.ldr * 2, 256, BR,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE) == cudaSuccess;
     static SmemLimit lim;
     e = raise_smem_limit(gemm_cm_kernel<BR, MODE, GK>, Cfg::SMEM, lim);
     if (e != cudaSuccess) return e;
@@ -676,8 +689,8 @@ static cudaError_t launch_cm_t(const GemmShape &g, const EpiParams &p, cudaStrea
                                           : (long)((g.M + BR - 1) / BR);
     const long tiles = (long)((g.N + 127) / 128) * row_tiles;
     const int grid = tiles < num_sms() ? (int)tiles : num_sms();
-    return launch_pdl(gemm_cm_kernel<BR, MODE, GK>, grid, kCmThreads, Cfg::SMEM, stream, tw, tx, g.M, g.N, g.K,
-                      g.win_rows, p);
+    return launch_pdl(gemm_cm_kernel<BR, MODE, GK>, grid, kCmThreads, Cfg::SMEM, stream, tw, tx, tr, g.M, g.N, g.K,
+                      g.win_rows, p, res_pf);
 }
 
 template <int MODE, int GK>

@@ -113,6 +113,14 @@ IW_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
                  : "memory");
 }
 
+// Bulk prefetch of one tile of a 2-D tensor map into L2 (no shared memory,
+// no completion to wait for).
+IW_DEV void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
 IW_DEV void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
