@@ -215,25 +215,6 @@ inline int num_sms() {
     return v;
 }
 
-// CTAs of `kernel` (threads per CTA, no dynamic shared memory) resident on
-// the whole current device: SMs x CTAs per SM, cached per device in `cache`
-// (one static array per kernel instantiation at the call site).
-template <typename... KArgs>
-inline int resident_ctas(void (*kernel)(KArgs...), int threads, std::atomic<int> (&cache)[kMaxDevices]) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-    const int slot = (dev >= 0 && dev < kMaxDevices) ? dev : 0;
-    int v = cache[slot].load(std::memory_order_relaxed);
-    if (v <= 0) {
-        int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm <= 0)
-            per_sm = 1;
-        v = per_sm * num_sms();
-        cache[slot].store(v, std::memory_order_relaxed);
-    }
-    return v;
-}
-
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                               Args &&...args) {
