@@ -112,6 +112,22 @@ def test_encode_batches_pipelined():
     for m, o in zip(mels, outs):
         want = model.encoder(m.cuda()).cpu()
         assert torch.equal(o, want)
+    # again with the graphs already captured (three batches, reversed), and at
+    # another batch size (its own buffers and graphs)
+    outs2 = [torch.empty_like(o).pin_memory() for o in outs[:3]]
+    model.encode_batches(mels[:3][::-1], outs2)
+    torch.cuda.synchronize()
+    for o, want in zip(outs2, outs[:3][::-1]):
+        assert torch.equal(o, want)
+    one = [m[1:].contiguous().pin_memory() for m in mels[:2]]
+    outs1 = [torch.empty(1, dims.n_audio_ctx, dims.n_audio_state, dtype=torch.int8).pin_memory() for _ in one]
+    model.encode_batches(one, outs1)
+    torch.cuda.synchronize()
+    for o, want in zip(outs1, outs[:2]):
+        assert torch.equal(o[0], want[1])
+    assert model.graph_launches[("encode_batches", 2)] > 0 and model.graph_launches[("encode_batches", 1)] > 0
+    with pytest.raises(RuntimeError):
+        model.encode_batches(mels[:1], [torch.empty(1, 3, dtype=torch.int8)])
 
 
 def test_encoder_from_audio():
