@@ -90,7 +90,7 @@ class GemmDesc(C.Structure):
         ("vt_out", _P), ("vt_ld", _I64), ("vt_col0", _I64), ("vt_T", _I64),
         ("kv_cache_k", _P), ("kv_cache_v", _P), ("kv_col0", _I64), ("kv_heads", _I64), ("kv_T", _I64),
         ("kv_Tcap", _I64), ("kv_pos", _I64), ("kv_pos_dev", _P), ("gelu_table_tiled", _P),
-        ("x_window_rows", _I64), ("x_window_stride", _I64),
+        ("x_window_rows", _I64), ("x_window_stride", _I64), ("weight_sign", _P),
     ]
 
 

@@ -398,6 +398,10 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     if (d->K % 16 || d->ldx % 16 || d->ldw % 16)
         return fail(IW_EINVAL, "iw_gemm_i8: K and the row strides must be multiples of 16");
     if (d->weight_zero && !d->x_rowsum) return fail(IW_EINVAL, "iw_gemm_i8: weight_zero needs x_rowsum");
+    if (d->weight_sign && d->weight_zero)
+        return fail(IW_EINVAL, "iw_gemm_i8: weight_sign is for folded zero points (weight_zero must be NULL)");
+    if (d->weight_sign && !iw::cm_enabled())
+        return fail(IW_EINVAL, "iw_gemm_i8: weight_sign needs the channel-major kernel");
     if (d->mode < 0 || d->mode > 3) return fail(IW_EINVAL, "iw_gemm_i8: bad mode %d", d->mode);
     if ((d->mode == IW_GEMM_LINEAR32 || d->mode == IW_GEMM_LINEAR32_RES) && (!d->multiplier || !d->shift))
         return fail(IW_EINVAL, "iw_gemm_i8: Linear32 needs per-channel multiplier and shift");
@@ -420,6 +424,7 @@ int iw_gemm_i8(const iw_gemm_desc *d, void *stream) {
     p.ldo = d->ldo;
     p.bias = d->bias;
     p.wz = d->weight_zero;
+    p.wsign = d->weight_sign;
     p.rowsum = d->x_rowsum;
     if (d->multiplier) {
         p.per_channel = 1;

@@ -25,6 +25,8 @@
 // batch (V^T for the attention's P.V operand, or [B, N, T]), int16 after
 // Residual15, int16 after the positional add-requant; optional per-row sums
 // of the int8 output for the next GEMM's zero point. All waits are bounded.
+#include <type_traits>
+
 #include "gemm_i8.cuh"
 #include "iw_common.cuh"
 #include "iw_sm100.cuh"
@@ -57,7 +59,8 @@ IW_DEV void cm_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCmEpiWarps * 32) : 
 
 // Everything the epilogue needs about its channel, loaded once per tile.
 struct ChanK {
-    int32_t bias, nwz, mul, hmask;  // acc + bias - wz*rowsum; mulh by u32 multiplier
+    int32_t bias, nwz, mul, hmask;  // sgn*acc + bias - wz*rowsum; mulh by u32 multiplier
+    int32_t sgn;                     // +1, or -1 for a channel whose folded weights are negated
     RrsK q;                          // Linear8: rrs shift; Linear32: {sh, z} of the left shift
     int32_t gmi, gmo;                // GeLU multipliers (gelu_scalar.cpp)
     RrsK gi, go;                     // GeLU shifts (clamped to [0, 32])
@@ -67,6 +70,7 @@ struct ChanK {
 
 IW_DEV ChanK load_chan(const EpiParams &p, int n, bool cv, int mode) {
     ChanK c{};
+    c.sgn = 1;
     c.q = {0, 0, 0, 0};
     c.gi = c.go = c.ps = {0, 0, 0, 0};
     if (!cv) return c;
@@ -80,6 +84,7 @@ IW_DEV ChanK load_chan(const EpiParams &p, int n, bool cv, int mode) {
     }
     c.bias = p.bias ? __ldg(p.bias + n) : 0;
     c.nwz = p.wz ? -(int32_t)__ldg(p.wz + n) : 0;
+    c.sgn = p.wsign ? (int32_t)__ldg(p.wsign + n) : 1;
     c.mul = (int32_t)m;
     c.hmask = (m >> 31) ? -1 : 0;
     if (mode == EPI_L8) {
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
             // epilogue warps take the same decision.
             cm_bar();
             if (et == 0) *stop_s = *abort_flag;
-            if (!(rs_bulk && m0 + BR <= Mt))
+            if (p.wz && !(rs_bulk && m0 + BR <= Mt))
                 for (int i = et; i < BR; i += kCmEpiWarps * 32)
                     rs_t[i] = (p.wz && m0 + i < Mt) ? __ldg(p.rowsum + m0 + i) : 0;
             if (GT && !gt_bulk) {
@@ -409,15 +414,24 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                     tmem_ld_wait();
                     const int4 *rs4 = reinterpret_cast<const int4 *>(rs_t + c * kCmCh);
                     int32_t v[kCmCh];
-                    if (simple) {
+                    // the simple epilogue's element chain from the zero-point-corrected
+                    // accumulator a; ZP: a = acc + bias - wz*rowsum, else a = sgn*acc + bias
+                    auto simple_chain = [&](auto zp) {
 #pragma unroll
                         for (int q = 0; q < kCmCh / 4; ++q) {
-                            const int4 r4 = rs4[q];
-                            const int32_t rs[4] = {r4.x, r4.y, r4.z, r4.w};
+                            int32_t rs[4] = {0, 0, 0, 0};
+                            if constexpr (decltype(zp)::value) {
+                                const int4 r4 = rs4[q];
+                                rs[0] = r4.x; rs[1] = r4.y; rs[2] = r4.z; rs[3] = r4.w;
+                            }
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
                                 const int j = 4 * q + u;
-                                const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                int32_t a;
+                                if constexpr (decltype(zp)::value)
+                                    a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                else
+                                    a = u_mad((int32_t)acc[j], ck.sgn, ck.bias);
                                 if constexpr (MODE != EPI_L8) {
                                     v[j] = (int32_t)((uint32_t)__mulhi(a, ck.mul) << ck.q.sh);
                                     continue;
@@ -432,6 +446,10 @@ __global__ void __launch_bounds__(kCmThreads, 1)
                                 v[j] = clampi(t >> ck.q.sh, -127, 127);
                             }
                         }
+                    };
+                    if (simple) {
+                        if (p.wz) simple_chain(std::true_type{});
+                        else simple_chain(std::false_type{});
                     } else {
 #pragma unroll
                         for (int q = 0; q < kCmCh / 4; ++q) {
@@ -440,7 +458,7 @@ __global__ void __launch_bounds__(kCmThreads, 1)
 #pragma unroll
                             for (int u = 0; u < 4; ++u) {
                                 const int j = 4 * q + u;
-                                const int32_t a = u_mad(ck.nwz, rs[u], u_add((int32_t)acc[j], ck.bias));
+                                const int32_t a = u_mad(ck.nwz, rs[u], u_mad((int32_t)acc[j], ck.sgn, ck.bias));
                                 const int32_t h = u_add(__mulhi(a, ck.mul), a & ck.hmask);
                                 if constexpr (MODE == EPI_L8) {
                                     v[j] = clampi(rrs_apply(h, ck.q), -127, 127);

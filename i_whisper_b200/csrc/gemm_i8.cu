@@ -593,8 +593,9 @@ cudaError_t gemm_i8_launch(const GemmShape &g, EpiMode mode, const EpiParams &p,
         if (cm_eligible(g, mode, q))
             return gemm_cm_launch(g, mode, q, stream, (bn_hint == 64 || bn_hint == 128 || bn_hint == 256) ? bn_hint : 0);
     }
-    // transposed and KV-cache outputs and windowed X need the channel-major kernel
-    if (p.tr_out || p.kv_k || g.win_rows > 0) return cudaErrorInvalidValue;
+    // transposed and KV-cache outputs, windowed X and accumulator signs need
+    // the channel-major kernel
+    if (p.tr_out || p.kv_k || g.win_rows > 0 || p.wsign) return cudaErrorInvalidValue;
     int bn = bn_hint;
     if (bn == 0) {
         // Prefer wide tiles; fall back to narrower ones when the grid would

@@ -23,6 +23,7 @@ struct EpiParams {
     // zero point / bias (Linear8/32, linear.py:50-97)
     const int32_t *bias = nullptr;    // [N]
     const int8_t *wz = nullptr;       // [N] weight zero points
+    const int8_t *wsign = nullptr;    // [N] +1/-1 applied to the accumulator (folded zero points; no wz)
     const int32_t *rowsum = nullptr;  // [M] sum of each X row (needed with wz)
     // requant: per channel (Linear8/32) or one scalar (conv, classifier)
     const uint32_t *mult = nullptr;   // [N]

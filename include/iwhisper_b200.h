@@ -289,6 +289,14 @@ typedef struct iw_gemm_desc {
      * Needs the channel-major kernel (IW_EINVAL otherwise). */
     int64_t x_window_rows;
     int64_t x_window_stride;
+    /* optional [N] int8, each +1 or -1: the accumulator of channel n is
+     * multiplied by weight_sign[n] before the bias is added (NULL = all +1).
+     * With weight_zero NULL it lets a caller fold a zero point into the
+     * weights exactly: w'[n][k] = s_n * (w[n][k] - wz[n]) gives
+     * s_n * acc' = acc - wz[n] * rowsum(x), so no row sums are needed; s_n
+     * is chosen per channel so that w' stays in [-128, 127]. Not with
+     * weight_zero (IW_EINVAL); needs the channel-major kernel. */
+    const int8_t *weight_sign;
 } iw_gemm_desc;
 
 /* tcgen05 (sm_100a) int8 GEMM with the epilogue described by *d. */

@@ -138,3 +138,26 @@ def test_graphed_encoder_equals_eager():
         assert torch.equal(got, ref), seeds
     assert model.graph_launches[("encoder", 2)] > 0
     assert _lib.device_status(clear=True) == 0
+
+
+def test_config0_zero_point_form_matches_folded():
+    """The zero-point form of every Linear_int (row sums produced by the
+    LayerNorms, the attention and fc1; the GEMMs subtracting wz * rowsum),
+    which the model keeps for checkpoints whose zero points do not fold into
+    int8 weights, gives config 0's golden bytes as the folded form does."""
+    from i_whisper_b200 import _lib
+    from i_whisper_b200.model import WhisperIntB200
+    g = json.load(open(GOLDEN))
+    try:
+        dims, sd = load_calibrated("tiny")
+    except FileNotFoundError as e:
+        pytest.skip(str(e))
+    model = WhisperIntB200(dims, sd, fold_zero_points=False)
+    assert all(L[k].wz is not None for L in model.enc_layers for k in ("qkv", "out", "fc1"))
+    c = g["tiny_config0"]
+    mel = synthetic_mel_batch(80, c["mel_seeds"], float(sd["encoder.input_alpha"][0]))
+    xa = model.encoder(torch.from_numpy(mel).cuda())
+    assert sha(xa) == c["encoder_sha256"]
+    toks = model.decode(xa, model._enc_ws[1]["rs_xa"], c["sample_len"], use_graph=True, stop_when_done=True)
+    assert toks.cpu().numpy().tolist() == c["tokens"]
+    assert _lib.device_status(clear=True) == 0

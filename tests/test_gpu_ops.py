@@ -697,6 +697,86 @@ def test_linear8_qkv_vt_out(ops, L, B, T, H):
     assert np.array_equal(host(vt)[:, :T], want_vt)
 
 
+def _foldable_linear(rng, M, K, N):
+    """A Linear_int whose zero points fold into int8 weights: channels whose
+    differences w - wz reach +128 (folded negated, sign -1), others reaching
+    -128 (kept, sign +1)."""
+    x = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    w = rng.integers(-100, 101, (N, K)).astype(np.int8)
+    wz = rng.integers(-27, 28, N).astype(np.int8)
+    w[::7, 0], wz[::7] = 127, -1
+    w[3::7, 1], wz[3::7] = -128, 0
+    b = rng.integers(-(2 ** 20), 2 ** 20, N, dtype=np.int32)
+    m = rng.integers(2 ** 30, 2 ** 31, N, dtype=np.uint32)
+    s = rng.integers(1, 12, N).astype(np.int8)
+    return x, w, b, wz, m, s
+
+
+@pytest.mark.parametrize("form", ["linear8", "linear8_gelu_table", "linear8_vt", "linear32_residual15"])
+@pytest.mark.parametrize("M,K,N", [(515, 1024, 1024), (130, 384, 1536), (7, 1280, 256)])
+def test_gemm_folded_zero_point(ops, L, form, M, K, N):
+    """iw_gemm_i8 with the zero point folded into the weights
+    (model.fold_zero_point: w' = s*(w - wz), weight_sign = s, no row sums)
+    returns exactly the zero-point form's result, for every epilogue the
+    model folds: Linear8, Linear8 + GeLU table, the QKV form with V^T, and
+    Linear32 + Residual15. weight_sign together with weight_zero is refused."""
+    import ctypes
+    from i_whisper_b200 import _lib
+    from i_whisper_b200.model import fold_zero_point
+    rng = np.random.default_rng(M + K + N + len(form))
+    x, w, b, wz, m, s = _foldable_linear(rng, M, K, N)
+    wf, sign = fold_zero_point(w, wz)
+    assert (sign == 1).any() and (sign == -1).any()
+    st = torch.cuda.current_stream().cuda_stream
+    keep = []
+    g = _lib.GemmDesc()
+    X, W, B_, Mu, S_, SG = dev(x), dev(wf), dev(b), dev(m), dev(s), dev(sign)
+    g.x, g.ldx, g.w, g.ldw, g.M, g.N, g.K = X.data_ptr(), K, W.data_ptr(), K, M, N, K
+    g.bias, g.multiplier, g.shift, g.weight_sign = B_.data_ptr(), Mu.data_ptr(), S_.data_ptr(), SG.data_ptr()
+    if form == "linear32_residual15":
+        r = rng.integers(-16383, 16384, (M, N), dtype=np.int16)
+        ref = L.residual15(L.linear32(x, w, b, wz, m, s), r, 40000)
+        out = dev(r.copy())  # in place, as the model runs it
+        g.mode, g.out, g.ldo = _lib.IW_GEMM_LINEAR32_RES, out.data_ptr(), N
+        g.residual, g.ldr, g.residual_multiplier = out.data_ptr(), N, 40000
+    else:
+        ref = L.linear8(x, w, b, wz, m, s)
+        out = torch.zeros(M, N, dtype=torch.int8, device="cuda")
+        g.mode, g.out, g.ldo = _lib.IW_GEMM_INT8, out.data_ptr(), N
+        if form == "linear8_gelu_table":
+            lut = rng.integers(0, 256, 16, dtype=np.uint8)
+            gpar = [lut, rng.integers(0, 256, N, dtype=np.uint8), rng.integers(-2, 34, N).astype(np.int8),
+                    rng.integers(0, 256, N, dtype=np.uint8), rng.integers(-2, 34, N).astype(np.int8)]
+            ref = L.gelu(ref, *gpar)
+            gp = [dev(a) for a in gpar]
+            tab = torch.empty(N, 256, dtype=torch.int8, device="cuda")
+            _lib.call("iw_gelu_table", *[t.data_ptr() for t in gp], N, N, N, tab.data_ptr(), st)
+            keep += gp + [tab]
+            g.gelu_table = tab.data_ptr()
+        if form == "linear8_vt":
+            if N % 64:
+                pytest.skip("V^T needs whole heads")
+            # one batch of M rows; the upper half of the channels (whole
+            # heads) leaves as V^T
+            vt_ld = (M + 15) // 16 * 16
+            c0 = N // 2 // 64 * 64
+            vt = torch.zeros(N - c0, vt_ld, dtype=torch.int8, device="cuda")
+            g.vt_out, g.vt_ld, g.vt_col0, g.vt_T = vt.data_ptr(), vt_ld, c0, M
+    _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(g), st))
+    got = host(out)
+    if form == "linear8_vt":
+        assert np.array_equal(got[:, :c0], ref[:, :c0])
+        assert np.array_equal(host(vt)[:, :M], ref[:, c0:].T)
+    else:
+        assert np.array_equal(got, ref)
+    Z = dev(wz)
+    rs = torch.zeros(M, dtype=torch.int32, device="cuda")
+    g.weight_zero, g.x_rowsum = Z.data_ptr(), rs.data_ptr()
+    with pytest.raises(_lib.IWhisperError, match="weight_sign"):
+        _lib.check(_lib.LIB.iw_gemm_i8(ctypes.byref(g), st))
+    assert _lib.device_status(clear=True) == 0
+
+
 @pytest.mark.parametrize("B,T,N", [(2, 1500, 768), (3, 37, 128)])
 def test_linear8_headmajor(ops, L, B, T, N):
     """Cross-attention K/V form: Linear8 stored head-major [N/64, B, T, 64]."""
