@@ -12,8 +12,8 @@
 //           difference to rowmax+1 goes through the shift-exp as a lookup
 //           table (built on the device with the same function, see
 //           shift_exp_table), the u8 probabilities are summed per row and
-//           written to shared memory in the tensor-core operand layout, and
-//           O += P V^T runs on the tensor cores (u8 x s8 -> s32).
+//           written to tensor memory (tcgen05.st) as the A operand of
+//           O += P V^T, which runs on the tensor cores (u8 x s8 -> s32).
 //   end:    O is normalised by FISR(rowsum)^2 and the AV requant, and written
 //           as int8 rows [b*T + t, h*64 + d].
 // The reference's online order (row max first, then exp and sum) is kept
@@ -67,18 +67,24 @@ constexpr int TAB_SMEM = (2 + TAB_MAX + 15) / 16 * 16;  // header + entries, 16-
 constexpr int Q_BYTES = BQ * 64;
 constexpr int K_BYTES = BK * 64;
 constexpr int V_BYTES = 64 * BK;
-constexpr int P_BYTES = BQ * BK;
+constexpr int P_COLS = BK / 4;      // TMEM columns of one P buffer (four u8 keys per column)
 // layout (offsets from the 1024-aligned base)
 constexpr int OFF_Q = 0;                          // two Q buffers
 constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
 constexpr int OFF_V = OFF_K + KST * K_BYTES;
-constexpr int OFF_P = OFF_V + VST * V_BYTES;      // two P buffers (1024-aligned)
-constexpr int OFF_RED = OFF_P + 2 * P_BYTES;      // 3 x [SLICES][BQ] int32 cross-warp row max / sum / output sum
+constexpr int OFF_RED = OFF_V + VST * V_BYTES;    // 3 x [SLICES][BQ] int32 cross-warp row max / sum / output sum
 constexpr int OFF_BAR = OFF_RED + 3 * SLICES * BQ * 4;
 constexpr int SMEM = 1024 + OFF_BAR + 512;
-constexpr uint32_t TMEM_COLS = 512;  // S at 0/128/256, O at 384/448
+// TMEM: S at 0/128/256, O at 384 (one buffer: a work item's epilogue reads
+// O before the softmax warps write the next item's first P), P at 448/480.
+// P lives in TMEM as the P.V MMA's A operand, written with tcgen05.st: no
+// generic-to-async proxy fence per block (a shared-memory P needed one, 6%
+// of the kernel's time).
+constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_O = 384;
-static_assert(OFF_V % 1024 == 0 && OFF_P % 1024 == 0, "swizzle-128 tiles need 1024-byte alignment");
+constexpr uint32_t TMEM_P = 448;
+static_assert(TMEM_O + 64 <= TMEM_P && TMEM_P + 2 * P_COLS <= TMEM_COLS && SBUF * BK <= (int)TMEM_O, "TMEM map");
+static_assert(OFF_V % 1024 == 0, "swizzle-128 tiles need 1024-byte alignment");
 }  // namespace attn
 
 struct AttnTcParams {
@@ -142,7 +148,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sK = smem + OFF_K;
     uint8_t *sV = smem + OFF_V;
-    uint8_t *sP = smem + OFF_P;
     // the shift-exp table lives in static shared memory: its address is a
     // compile-time constant, so a lookup is one load with an immediate offset
     __shared__ __align__(16) uint8_t sTabRaw[TAB_SMEM];
@@ -284,20 +289,21 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                 }
             } else {
                 constexpr uint32_t idesc_pv = idesc_i8(BQ, 64, false, true);
-                int pb = 0, vs = 0, ob = 0;
+                int pb = 0, vs = 0;
+                constexpr int ob = 0;  // one O buffer
                 uint32_t pph = 0, vph = 0, oph = 0;
                 for (int it = blockIdx.x; it < items && ok && !*abort_flag; it += gridDim.x) {
                     for (int j = 0; j < nkb; ++j) {
                         if (!mbar_wait(&p_full[pb], pph) || !mbar_wait(&v_full[vs], vph)) { ok = false; break; }
                         if (j == 0 && !mbar_wait(&o_empty[ob], oph ^ 1)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t pa = smem_u32(sP + pb * P_BYTES);
+                        const uint32_t tp = tmem_base + TMEM_P + (uint32_t)(pb * P_COLS);
                         const uint32_t va = smem_u32(sV + vs * V_BYTES);
-                        const uint32_t tO = tmem_base + TMEM_O + (uint32_t)(ob * 64);
+                        const uint32_t tO = tmem_base + TMEM_O;
 #pragma unroll
                         for (int kk = 0; kk < BK / 32; ++kk)
-                            mma_i8(tO, sdesc_kmajor_sw128(pa + kk * 32), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
-                                   (j | kk) != 0);
+                            mma_i8_ts(tO, tp + (uint32_t)(kk * 8), sdesc_kmajor_sw128(va + kk * 32), idesc_pv,
+                                      (j | kk) != 0);
                         mma_commit(&v_empty[vs]);
                         mma_commit(&p_empty[pb]);
                         if (++vs == VST) { vs = 0; vph ^= 1; }
@@ -305,7 +311,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     }
                     if (!ok) break;
                     mma_commit(&o_full[ob]);
-                    if (++ob == 2) { ob = 0; oph ^= 1; }
+                    oph ^= 1;  // one O buffer (ob stays 0)
                 }
             }
             if (!ok) *abort_flag = 1;
@@ -345,7 +351,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const uint32_t col = (uint32_t)(slice * SC);
         const RrsK k_rsq = rrs_k(p.rsqrt_offset), k_av = rrs_k(p.av_shift);  // output normalisation shifts
         const bool epi_simple = k_rsq.sgn == -1 && k_av.sgn == -1;  // both shifts in [1, 31]
-        int sb = 0, pb = 0, ob = 0;
+        int sb = 0, pb = 0;
+        constexpr int ob = 0;  // one O buffer
         uint32_t sph = 0, pph = 0, oph = 0;
         // wait helper: every lane waits (the warp stays converged, which
         // measured faster than one lane waiting for the others), the warp
@@ -458,18 +465,15 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         exp_half(acc[hf], T - (j * BK + slice * SC + hf * 32), w4[hf], rsum);
                     // the P buffer must be free (P.V of block j-2 done)
                     if (!wait_all(&p_empty[pb], pph ^ 1)) break;
-                    // 16-byte chunks of this row; 128-byte swizzle: chunk k of
-                    // row r lives at chunk (k ^ (r & 7))
-                    uint8_t *prow = sP + pb * P_BYTES + r * 128;
+                    // this warp's 32 rows x SC keys of P: row = TMEM lane,
+                    // keys 4c..4c+3 in column c (the A operand's K-major layout)
 #pragma unroll
-                    for (int hf = 0; hf < HALVES; ++hf) {
-                        const int ch0 = slice * (SC / 16) + hf * 2;
-                        *reinterpret_cast<uint4 *>(prow + (((ch0) ^ (r & 7)) << 4)) =
-                            make_uint4(w4[hf][0], w4[hf][1], w4[hf][2], w4[hf][3]);
-                        *reinterpret_cast<uint4 *>(prow + (((ch0 + 1) ^ (r & 7)) << 4)) =
-                            make_uint4(w4[hf][4], w4[hf][5], w4[hf][6], w4[hf][7]);
-                    }
-                    fence_proxy_async_smem();
+                    for (int hf = 0; hf < HALVES; ++hf)
+                        tmem_st_32x32b_x8(tmem_base + lane_base + TMEM_P +
+                                              (uint32_t)(pb * P_COLS + (slice * SC + hf * 32) / 4),
+                                          w4[hf]);
+                    tmem_st_wait();
+                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&p_full[pb]);
                     if (++sb == SBUF) { sb = 0; sph ^= 1; }
@@ -516,10 +520,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     tc_fence_after();
                     uint32_t acc[OC];
                     if constexpr (OC == 32)
-                        tmem_ld_32x32b_x32(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                        tmem_ld_32x32b_x32(tmem_base + lane_base + TMEM_O + (uint32_t)(slice * OC),
                                            *reinterpret_cast<uint32_t (*)[32]>(acc));
                     else
-                        tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(ob * 64 + slice * OC),
+                        tmem_ld_32x32b_x16(tmem_base + lane_base + TMEM_O + (uint32_t)(slice * OC),
                                            *reinterpret_cast<uint32_t (*)[16]>(acc));
                     tmem_ld_wait();
                     tc_fence_before();
@@ -566,7 +570,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                         }
                     }
                 }
-                if (++ob == 2) { ob = 0; oph ^= 1; }
+                oph ^= 1;  // one O buffer (ob stays 0)
                 if (p.rowsum_out) {
                     // one atomic per row and head: slice-0 warps add the slices' sums
                     bar_soft();
