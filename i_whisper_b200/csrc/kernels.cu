@@ -869,97 +869,132 @@ static cudaError_t attention_cc_launch(const AttnArgs &a, int B, int H, cudaStre
     return launch_pdl(attn_cc_kernel<QB, RING>, grid, kAttnThreads, smem, st, a);
 }
 
-// One decode query (Tq == 1) over a short key sequence (at most 32*KPL
-// keys): one warp per (batch, head), no block barriers. Lane l scores keys
-// l, l+32, ... (64-byte rows, 16 dp4a each) and keeps them in registers;
-// for P.V the two half-warps take alternate keys and lane l accumulates
-// dims 4*(l%16)..+3, the probabilities broadcast by shuffles. Same integer
-// steps as attn_cc_kernel (qk_requant_rowmax, shift_exp, pv_norm_requant).
-// Measured 2x faster per launch than attn_cc_kernel<1> on the decoder's
-// self-attention (256 utterances, up to 131 keys).
-constexpr int kAttnWarpCta = 8;  // warps per CTA
-template <int KPL>
-__global__ void __launch_bounds__(32 * kAttnWarpCta) attn_warp_kernel(AttnArgs a, int B, int H) {
+// One decode query (Tq == 1) over at most 512 keys. A CTA of eight warps
+// serves G = 1, 2, 4 or 8 warps per (batch, head), chosen on the device from
+// the key count (the smallest G with Tk <= 32*G; 8 above 128 keys), so 8/G
+// pairs per CTA. Warp s of a pair takes keys s*32 + lane (and 256 + s*32 +
+// lane when Tk > 256) and issues its key rows (16-byte loads, lane = key)
+// and the value rows of the same 32 keys (4-byte loads, half-warp = one
+// 64-byte row) before any arithmetic, so a pair costs one memory round trip
+// instead of one per group of keys. Row max and row sum combine across the
+// pair's warps in shared memory, and so do the int32 P.V partials (integer
+// sums: the order does not change them). Same integer steps as
+// attn_cc_kernel (qk_requant_rowmax, shift_exp, pv_norm_requant).
+constexpr int kAttnDecWarps = 8;
+__global__ void __launch_bounds__(32 * kAttnDecWarps, 4) attn_dec_kernel(AttnArgs a, int B, int H) {
     pdl_wait();
     pdl_launch();
-    const int lane = threadIdx.x & 31;
-    const int pair = blockIdx.x * kAttnWarpCta + (threadIdx.x >> 5);
-    if (pair >= B * H) return;
-    const int b = pair / H, h = pair - (pair / H) * H;
+    __shared__ int32_t s_red[2][kAttnDecWarps];
+    __shared__ int32_t s_pv[kAttnDecWarps][64];
     const int Tk = a.Tk_dev ? *a.Tk_dev : a.Tk;
+    const int G = Tk <= 32 ? 1 : Tk <= 64 ? 2 : Tk <= 128 ? 4 : 8;  // warps per pair (CTA-uniform)
+    const int per = kAttnDecWarps / G;                              // pairs per CTA
+    if ((int)blockIdx.x * per >= B * H) return;  // the whole CTA, before any barrier
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int hw = lane >> 4, dl = lane & 15;
+    const int pl = w / G, sub = w - pl * G;      // pair within the CTA, warp within the pair
+    const int pair = (int)blockIdx.x * per + pl;
+    const bool live = pair < B * H;              // warp-uniform
+    const int b = live ? pair / H : 0, h = live ? pair - (pair / H) * H : 0;
+    const int8_t *kb = a.k + (int64_t)b * a.k_bs + (int64_t)h * a.k_hs;
+    const int8_t *vb = a.v + (int64_t)b * a.v_bs + (int64_t)h * a.v_hs + 4 * dl;
     const int8_t *qp = a.q + (int64_t)b * a.q_bs + (int64_t)h * a.q_hs;
+    const int kt = live ? Tk : 0;                // keys this warp may read
+    // round 0: this warp's keys and their value rows, all loads in flight
+    const int j0 = sub * 32 + lane;
+    int4 kk[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) kk[c] = j0 < kt ? ld_nc_v4(kb + (int64_t)j0 * a.ldk + 16 * c) : make_int4(0, 0, 0, 0);
+    int32_t vw[16];
+#pragma unroll
+    for (int s2 = 0; s2 < 16; ++s2) {
+        const int j = sub * 32 + 2 * s2 + hw;
+        vw[s2] = j < kt ? __ldg(reinterpret_cast<const int32_t *>(vb + (int64_t)j * a.ldv)) : 0;
+    }
     int4 qv[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) qv[c] = *reinterpret_cast<const int4 *>(qp + 16 * c);
-    const int8_t *kb = a.k + (int64_t)b * a.k_bs + (int64_t)h * a.k_hs;
+    for (int c = 0; c < 4; ++c) qv[c] = live ? *reinterpret_cast<const int4 *>(qp + 16 * c) : make_int4(0, 0, 0, 0);
     const uint32_t qsh = (uint32_t)(a.qk_shift > 0 ? a.qk_shift : 0);
-    // scores (int16 after the requant; -32768 for masked or missing keys)
-    int32_t sv[KPL];
-    int32_t lmax = -32768;
+    // score of key j (int16 after the requant; -32768 when masked or missing)
+    auto score = [&](int j, const int4 (&k4)[4]) -> int32_t {
+        if (j >= kt || (a.mask_mode == 2 && a.mask[j] != 0)) return -32768;
+        int32_t acc = 0;
 #pragma unroll
-    for (int i = 0; i < KPL; ++i) {
-        const int j = i * 32 + lane;
-        sv[i] = -32768;
-        if (j < Tk) {
-            const int8_t *kr = kb + (int64_t)j * a.ldk;
-            int32_t acc = 0;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int4 kk = ld_nc_v4(kr + 16 * c);
-                acc = __dp4a(kk.x, qv[c].x, acc);
-                acc = __dp4a(kk.y, qv[c].y, acc);
-                acc = __dp4a(kk.z, qv[c].z, acc);
-                acc = __dp4a(kk.w, qv[c].w, acc);
-            }
-            // Tq == 1: the query sits at position Tk - 1, so a causal mask hides nothing
-            const bool masked = a.mask_mode == 2 && a.mask[j] != 0;
-            if (!masked) {
-                sv[i] = clampi(rrs(wmul(acc, (int32_t)a.qk_mult), qsh), -32768, 32767);
-                lmax = max(lmax, sv[i]);
-            }
+        for (int c = 0; c < 4; ++c) {
+            acc = __dp4a(k4[c].x, qv[c].x, acc);
+            acc = __dp4a(k4[c].y, qv[c].y, acc);
+            acc = __dp4a(k4[c].z, qv[c].z, acc);
+            acc = __dp4a(k4[c].w, qv[c].w, acc);
         }
-    }
-    const int32_t rmax1 = (int16_t)(warp_max(lmax) + 1);  // int16 wrap of row max + 1
-    int32_t e[KPL];
-    int32_t lsum = 0;
+        // Tq == 1: the query sits at position Tk - 1, so a causal mask hides nothing
+        return clampi(rrs(wmul(acc, (int32_t)a.qk_mult), qsh), -32768, 32767);
+    };
+    const int32_t sv0 = score(j0, kk);
+    const bool two = Tk > 32 * kAttnDecWarps;  // CTA-uniform (G == 8)
+    const int j1 = 32 * kAttnDecWarps + j0;
+    int32_t sv1 = -32768;
+    if (two) {
 #pragma unroll
-    for (int i = 0; i < KPL; ++i) {
-        const int j = i * 32 + lane;
-        const bool masked = j >= Tk || (a.mask_mode == 2 && a.mask[j] != 0);
-        e[i] = masked ? 0 : shift_exp_one(sv[i], rmax1, a.frac_bits);
-        lsum += e[i];
+        for (int c = 0; c < 4; ++c) kk[c] = j1 < kt ? ld_nc_v4(kb + (int64_t)j1 * a.ldk + 16 * c) : make_int4(0, 0, 0, 0);
+        sv1 = score(j1, kk);
     }
-    const int32_t rowsum = warp_sum(lsum);
+    // masked and missing keys hold -32768, which leaves the max of the
+    // unmasked scores unchanged (-32768 for a row with none, as in the
+    // reference's qk_requant_rowmax)
+    int32_t m = warp_max(max(sv0, sv1));
+    if (lane == 0) s_red[0][w] = m;
+    __syncthreads();
+    m = s_red[0][pl * G];
+    for (int i = 1; i < G; ++i) m = max(m, s_red[0][pl * G + i]);
+    const int32_t rmax1 = (int16_t)(m + 1);  // int16 wrap of row max + 1
+    auto pexp = [&](int j, int32_t sv) -> int32_t {
+        const bool masked = j >= kt || (a.mask_mode == 2 && a.mask[j] != 0);
+        return masked ? 0 : shift_exp_one(sv, rmax1, a.frac_bits);
+    };
+    const int32_t e0 = pexp(j0, sv0);
+    const int32_t e1 = two ? pexp(j1, sv1) : 0;
+    const int32_t ls = warp_sum(e0 + e1);
+    if (lane == 0) s_red[1][w] = ls;
     // P.V: half-warp hw takes keys of parity hw, lane accumulates dims 4*dl..4*dl+3
-    const int hw = lane >> 4, dl = lane & 15;
-    const int8_t *vb = a.v + (int64_t)b * a.v_bs + (int64_t)h * a.v_hs + 4 * dl;
     int32_t acc4[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int i = 0; i < KPL; ++i) {
-        if (i * 32 < Tk) {  // warp-uniform
-            const int32_t ei = e[i];
-#pragma unroll 8
-            for (int s2 = 0; s2 < 32; s2 += 2) {
-                const int src = s2 + hw;
-                const uint32_t pj = (uint32_t)__shfl_sync(0xffffffffu, ei, src);
-                const int j = i * 32 + src;
-                if (pj != 0) {  // zero-probability keys (and keys past Tk) are not read
-                    const int32_t vw = __ldg(reinterpret_cast<const int32_t *>(vb + (int64_t)j * a.ldv));
+    for (int s2 = 0; s2 < 16; ++s2) {
+        const uint32_t pj = (uint32_t)__shfl_sync(0xffffffffu, e0, 2 * s2 + hw);
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) acc4[c] = dp4a_us(pj << (8 * c), vw, acc4[c]);
-                }
-            }
+        for (int c = 0; c < 4; ++c) acc4[c] = dp4a_us(pj << (8 * c), vw[s2], acc4[c]);
+    }
+    if (two) {
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+            const int j = 32 * kAttnDecWarps + sub * 32 + 2 * s2 + hw;
+            vw[s2] = j < kt ? __ldg(reinterpret_cast<const int32_t *>(vb + (int64_t)j * a.ldv)) : 0;
+        }
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+            const uint32_t pj = (uint32_t)__shfl_sync(0xffffffffu, e1, 2 * s2 + hw);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc4[c] = dp4a_us(pj << (8 * c), vw[s2], acc4[c]);
         }
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc4[c] += __shfl_xor_sync(0xffffffffu, acc4[c], 16);
+    if (hw == 0) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s_pv[w][4 * dl + c] = acc4[c];
+    }
+    __syncthreads();
+    if (sub != 0 || !live) return;
+    int32_t rowsum = 0;
+    for (int i = 0; i < G; ++i) rowsum += s_red[1][pl * G + i];
     const int32_t inv = fisr(rowsum, a.rsqrt_offset);
     const uint32_t avs = (uint32_t)clampi(a.av_shift, 0, 32);
     uint32_t packed = 0;
     int32_t osum = 0;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        int32_t v = rrs(wmul(acc4[c], inv), a.rsqrt_offset);
+        uint32_t sum = 0;
+        for (int i = 0; i < G; ++i) sum += (uint32_t)s_pv[pl * G + i][4 * dl + c];
+        int32_t v = rrs(wmul((int32_t)sum, inv), a.rsqrt_offset);
         v = rrs(wmul(v, inv), a.rsqrt_offset);
         v = rrs(wmul(v, (int32_t)a.av_mult), avs);
         v = clampi(v, -127, 127);
@@ -974,27 +1009,18 @@ __global__ void __launch_bounds__(32 * kAttnWarpCta) attn_warp_kernel(AttnArgs a
     }
 }
 
-template <int KPL>
-static cudaError_t attention_warp_launch(const AttnArgs &a, int B, int H, cudaStream_t st) {
-    const int pairs = B * H;
-    return launch_pdl(attn_warp_kernel<KPL>, (pairs + kAttnWarpCta - 1) / kAttnWarpCta, 32 * kAttnWarpCta, 0, st, a,
-                      B, H);
-}
-
 cudaError_t attention_cc(const AttnArgs &a, int B, int H, cudaStream_t st) {
     if (B <= 0 || H <= 0 || a.Tq <= 0) return cudaSuccess;
     // single decode query over a short key sequence (decoder self-attention):
-    // one warp per (batch, head); 4-byte V loads need 4-byte aligned rows
+    // one to eight warps per (batch, head); 4-byte V loads need 4-byte
+    // aligned rows, 16-byte K and Q loads 16-byte aligned ones
     const int cap = a.Tk_cap > 0 ? a.Tk_cap : a.Tk;
     const bool v_al = ((reinterpret_cast<uintptr_t>(a.v) | (uintptr_t)a.ldv | (uintptr_t)a.v_bs | (uintptr_t)a.v_hs) & 3) == 0;
     const bool o_al = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)a.o_bs | (uintptr_t)a.o_hs) & 3) == 0;
     const bool k_al = ((reinterpret_cast<uintptr_t>(a.k) | (uintptr_t)a.ldk | (uintptr_t)a.k_bs | (uintptr_t)a.k_hs) & 15) == 0 &&
                       ((reinterpret_cast<uintptr_t>(a.q) | (uintptr_t)a.q_bs | (uintptr_t)a.q_hs) & 15) == 0;
-    if (a.Tq == 1 && cap <= 512 && v_al && o_al && k_al) {
-        if (cap <= 128) return attention_warp_launch<4>(a, B, H, st);
-        if (cap <= 256) return attention_warp_launch<8>(a, B, H, st);
-        return attention_warp_launch<16>(a, B, H, st);
-    }
+    if (a.Tq == 1 && cap <= 512 && v_al && o_al && k_al)
+        return launch_pdl(attn_dec_kernel, B * H, 32 * kAttnDecWarps, 0, st, a, B, H);
     // one query row per CTA for decode steps; four otherwise (each CTA
     // re-reads K and V of its head, so wider query blocks save traffic)
     // (the K ring pays from ~1000 keys: measured on decode cross-attention

@@ -254,7 +254,13 @@ def test_pv_norm_negative_rowsum_raises(ops):
 
 @pytest.mark.parametrize("B,H,Tq,Tk,mode", [(2, 6, 1, 1500, 0), (3, 16, 1, 37, 1), (2, 8, 3, 3, 1), (1, 6, 40, 300, 0),
                                             (2, 4, 5, 9, 2), (1, 16, 130, 130, 0), (1, 2, 1, 1, 0), (2, 3, 2, 257, 0),
-                                            (2, 3, 2, 257, 2), (1, 4, 1, 448, 1)])
+                                            (2, 3, 2, 257, 2), (1, 4, 1, 448, 1),
+                                            # one decode query: 1, 2, 4 or 8 warps per (batch, head) by key
+                                            # count, both sides of each boundary, the second key round past
+                                            # 256 keys, explicit masks, 15 pairs (a part-filled last CTA)
+                                            (3, 5, 1, 32, 0), (3, 5, 1, 33, 2), (3, 5, 1, 64, 1), (3, 5, 1, 65, 0),
+                                            (3, 5, 1, 128, 2), (3, 5, 1, 129, 1), (3, 5, 1, 256, 0),
+                                            (3, 5, 1, 300, 2), (2, 5, 1, 512, 0)])
 def test_fused_attention(ops, L, B, H, Tq, Tk, mode):
     rng = np.random.default_rng(B + H + Tq + Tk + mode)
     d = H * 64
