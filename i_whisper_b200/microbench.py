@@ -12,6 +12,7 @@ summaries are taken with (small cases, one kernel per process).
     python -m i_whisper_b200.microbench layernorm --rows 1500 --d 1024
     python -m i_whisper_b200.microbench attention --B 4 --H 16 --T 1500
     python -m i_whisper_b200.microbench cross_attention --B 256 --H 16 --T 1500
+    python -m i_whisper_b200.microbench decode --B 256 --from-step 96
 
 Input distributions follow the benchmark configuration: INT8 entries uniform
 in [-127, 127]; per-channel scales uniform in [1e-3, 1e-2] turned into
@@ -228,9 +229,42 @@ def bench_frontend(B: int, n_mels: int, reps: int, seed: int) -> dict:
             "peak_source": src}
 
 
+def bench_decode(B: int, n0: int, model: str = "medium", seed: int = 0) -> dict:
+    """Greedy decode steps of the reference-calibrated checkpoint over B
+    utterances (seeded random INT8 mel): the time of steps n0 .. n0+32 as
+    t(decode of n0 + 32 steps) - t(decode of n0 steps), best of three, each
+    step one CUDA-graph replay (self-attention over n0+3 .. n0+35 keys)."""
+    from .checkpoint import load_calibrated
+    from .model import WhisperIntB200
+    dims, sd = load_calibrated(model)
+    m = WhisperIntB200(dims, sd)
+    del sd
+    g = torch.Generator().manual_seed(seed)
+    mel = torch.randint(-60, 60, (B, dims.n_mels, 2 * dims.n_audio_ctx), dtype=torch.int8, generator=g).cuda()
+    xa = m.encoder(mel)
+    rs = m._enc_ws[B]["rs_xa"]
+
+    def run(n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        m.decode(xa, rs, n, use_graph=True)
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    n1 = n0 + 32
+    run(n0), run(n1)  # graph capture
+    ms = (min(run(n1) for _ in range(3)) - min(run(n0) for _ in range(3))) / 32
+    return {"op": "decode", "model": model, "B": B, "steps": [n0, n1], "ms_per_step": round(ms, 4),
+            "tok_per_s": round(B / ms * 1e3, 1)}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    p.add_argument("op", choices=["gemm", "layernorm", "attention", "cross_attention", "frontend"])
+    p.add_argument("op", choices=["gemm", "layernorm", "attention", "cross_attention", "frontend", "decode"])
+    p.add_argument("--model", default="medium", help="decode: calibrated checkpoint size")
+    p.add_argument("--from-step", type=int, default=16, help="decode: first timed step")
     p.add_argument("--n-mels", type=int, default=80)
     p.add_argument("--M", type=int, default=12000)
     p.add_argument("--K", type=int, default=1024)
@@ -263,6 +297,8 @@ def main(argv=None):
         r = bench_attention(a.B, a.H, a.T, a.reps, a.seed, a.qk_mult, a.qk_shift, a.frac_bits, a.std)
     elif a.op == "frontend":
         r = bench_frontend(a.B, a.n_mels, a.reps, a.seed)
+    elif a.op == "decode":
+        r = bench_decode(a.B, a.from_step, a.model, a.seed)
     else:
         r = bench_cross_attention(a.B, a.H, a.T, a.reps, a.seed)
     if _lib.device_status(clear=True) != 0:
