@@ -72,3 +72,30 @@ def test_reference_arm_follows_the_config():
     d1 = json.loads([ln for ln in r1.stdout.splitlines() if ln.startswith("{")][0])
     assert d1["unit"] == "TOPS" and d1["value"] > 0 and d1["config"]["baseline_config"] == 1
     assert d1["cpu_baseline"]["cores"] == 1 and d1["e2e"]["unit"] == "TOPS"
+
+
+def test_parity_check_compares_the_decoded_prefix():
+    """A run that decodes fewer tokens than the golden holds is checked on
+    the tokens it has (and a wrong one among them still fails)."""
+    import hashlib
+
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    xa = torch.arange(2 * 6, dtype=torch.int8).reshape(2, 2, 3)
+    sha = [hashlib.sha256(xa[i].numpy().tobytes()).hexdigest() for i in range(2)]
+    gold_toks = [[50258, 50259, 50359, 11, 12, 13, 14, 15], [50258, 50259, 50359, 21, 22, 23, 24, 25]]
+    golden = {"mel_seeds": [0, 1], "encoder_sha256": sha, "tokens": gold_toks, "sample_len": 5}
+    short = torch.tensor([t[:5] for t in gold_toks])
+    r = bench.check_parity(golden, xa, short, [0, 1])
+    assert r["ok"] and r["windows"] == [0, 1]
+    full = torch.tensor(gold_toks)
+    assert bench.check_parity(golden, xa, full, [0, 1])["ok"]
+    bad = short.clone()
+    bad[1, 4] = 99
+    r = bench.check_parity(golden, xa, bad, [0, 1])
+    assert not r["ok"] and r["mismatches"] == [{"window": 1, "encoder": True, "tokens": False}]
+    assert np.array_equal(bad[0].numpy(), short[0].numpy())
