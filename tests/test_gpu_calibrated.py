@@ -16,7 +16,9 @@ qk multipliers 64-127 with shifts 6-8, per-channel GeLU shifts 11-18 and so on.
 * whisper-medium at the benchmark's batch of 256 windows (M = 384000-row
   GEMMs, the persistent schedules over ~1500 tiles per SM wave, an 18.9 GB
   head-major cross-K/V cache): windows 0 and 1 of the batch reproduce the
-  same oracle digests and tokens, and the last window equals a batch-1 run.
+  same oracle digests and tokens, and the last window equals a batch-1 run;
+* whisper-small and whisper-large, one window each, against the oracle
+  (encoder output, 8 greedy tokens).
 """
 import hashlib
 import json
@@ -159,5 +161,25 @@ def test_config0_zero_point_form_matches_folded():
     xa = model.encoder(torch.from_numpy(mel).cuda())
     assert sha(xa) == c["encoder_sha256"]
     toks = model.decode(xa, model._enc_ws[1]["rs_xa"], c["sample_len"], use_graph=True, stop_when_done=True)
+    assert toks.cpu().numpy().tolist() == c["tokens"]
+    assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("size", ["small", "large"])
+def test_small_and_large_match_oracle(size):
+    """whisper-small (12 + 12 layers, d = 768) and whisper-large (32 + 32
+    layers, d = 1280, 128 mel bins, the 51866-token vocabulary) on their
+    calibrated checkpoints: the seed-0 window's encoder output and 8 greedy
+    tokens equal the oracle's (the windows BASELINE configurations 2 and 4
+    start from)."""
+    from i_whisper_b200 import _lib
+    model, sd, g = calibrated_model(size)
+    c = g[f"{size}_w1"]
+    mel = synthetic_mel_batch(model.dims.n_mels, c["mel_seeds"], float(sd["encoder.input_alpha"][0]))
+    assert [sha(m) for m in mel] == c["mel_sha256"]
+    xa = model.encoder(torch.from_numpy(mel).cuda())
+    for b in range(len(mel)):
+        assert sha(xa[b]) == c["encoder_sha256"][b], f"window {b}"
+    toks = model.decode(xa, model._enc_ws[len(mel)]["rs_xa"], c["sample_len"], use_graph=True)
     assert toks.cpu().numpy().tolist() == c["tokens"]
     assert _lib.device_status(clear=True) == 0
